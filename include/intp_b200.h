@@ -1,0 +1,134 @@
+/*
+ * intp_b200.h - C ABI of the B200 (sm_100a) Look-attention and negative-L1 library.
+ *
+ * The reference (Hevensh/INTP_Preliminary) is pure Python + Triton, so it has no
+ * native FFI of its own.  Each entry point below replaces one Python-level
+ * launch site of the reference and takes exactly the arguments that site hands
+ * to its Triton kernel: raw device pointers, element strides, sizes, a dtype
+ * code and the CUDA stream.  No torch type crosses this boundary, no C++
+ * exception escapes it, and the library never allocates or frees caller memory.
+ *
+ * Every function returns an intp_status (0 = success).
+ */
+#ifndef INTP_B200_H
+#define INTP_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define INTP_API __attribute__((visibility("default")))
+#else
+#define INTP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+typedef int32_t intp_status;
+#define INTP_OK               0
+#define INTP_ERR_ARGUMENT     1  /* null pointer or inconsistent sizes          */
+#define INTP_ERR_SHAPE        2  /* shape rule of the reference violated        */
+#define INTP_ERR_DTYPE        3  /* unsupported dtype code                      */
+#define INTP_ERR_LAYOUT       4  /* stride / alignment the kernel cannot take   */
+#define INTP_ERR_ARCH         5  /* device is not sm_100 (B200)                 */
+#define INTP_ERR_LAUNCH       6  /* CUDA runtime error at launch                */
+#define INTP_ERR_TIMEOUT      7  /* a bounded device wait gave up (see status)  */
+#define INTP_ERR_UNSUPPORTED  8  /* valid request outside the kernel's coverage */
+
+/* ---- dtype codes --------------------------------------------------------- */
+#define INTP_F32   0
+#define INTP_F16   1
+#define INTP_BF16  2
+
+/* ---- Look-bias modes ------------------------------------------------------ */
+/* NONE    : plain softmax attention (no Look bias).
+ * FIELDS  : the reference's general form: bias[b,h,i,j] =
+ *           sum_p pose[b,i-1,h,p] * fields[h,p,i-1,j-1] for i,j >= 1.
+ * SLOTS   : the same bias when fields[h,p,q,k] is the one-hot indicator of a
+ *           per-pair slot index: bias[b,h,i,j] = pose[b,i-1,h,slot(i,j)]
+ *           (zero where the pair has no slot).  The pair table is prepared
+ *           once by sla_pack_slot_table and shared by every batch and head.  */
+#define SLA_BIAS_NONE    0
+#define SLA_BIAS_FIELDS  1
+#define SLA_BIAS_SLOTS   2
+
+/* Slot value meaning "no Look bias for this pair" in an unpacked slot table. */
+#define SLA_SLOT_NONE 255
+
+/* Kernel selection (sla_forward_args.kernel). */
+#define SLA_KERNEL_AUTO      0   /* tcgen05 path when it applies, else SIMT     */
+#define SLA_KERNEL_SIMT      1   /* CUDA-core path (every dtype, mode, layout)  */
+#define SLA_KERNEL_TCGEN05   2   /* tensor-core path; fails if it cannot apply  */
+
+/* Arguments of one structured-Look-attention forward.
+ *
+ * Tensors follow the reference layouts (layers/triton_structured_look_attention.py:412-424):
+ *   q, k, v, out : (B, H, N, D), N = Np + 1 (token 0 is CLS), any strides, D stride 1
+ *   pose         : (B, Np, H, P) floating, any strides
+ *   fields       : (H, P, Np, Np) floating (FIELDS mode only), any strides
+ *   dense        : (B, H, Np, Np) floating or NULL, any strides
+ *   lse          : (B, H, N) float32 contiguous, or NULL when not wanted
+ * Strides are in elements.  In SLOTS mode `slots_packed` / `slot_tile_flags`
+ * come from sla_pack_slot_table for this N and are device pointers.          */
+typedef struct sla_forward_args {
+  int64_t batch, heads, seq, head_dim;
+  float scale;
+  int32_t dtype;                 /* dtype of q, k, v and out                  */
+  const void* q; int64_t q_stride[4];
+  const void* k; int64_t k_stride[4];
+  const void* v; int64_t v_stride[4];
+  void* out;     int64_t out_stride[4];
+  float* lse;
+  int32_t bias_mode;
+  int64_t poses;                 /* P (FIELDS) or number of slots (SLOTS)     */
+  const void* pose;   int64_t pose_stride[4];   int32_t pose_dtype;
+  const void* fields; int64_t fields_stride[4]; int32_t fields_dtype;
+  const uint8_t* slots_packed;
+  const uint8_t* slot_tile_flags;
+  const void* dense;  int64_t dense_stride[4];  int32_t dense_dtype;
+  int32_t* status;               /* device int32: bounded-wait error word     */
+  int32_t kernel;                /* SLA_KERNEL_*                              */
+} sla_forward_args;
+
+/* Structured Look attention forward.
+ * Replaces the launch of `_structured_look_forward` in
+ * `_StructuredLookAttention.forward` (layers/triton_structured_look_attention.py:297-338),
+ * reached through `structured_look_attention` (:412-424).  `stream` is a
+ * cudaStream_t.  The call is asynchronous; device-side wait failures are
+ * reported through *args->status (read it with sla_read_status).            */
+INTP_API intp_status sla_forward(const sla_forward_args* args, void* stream);
+
+/* Bytes needed by the packed slot table and the tile flags for sequence N. */
+INTP_API intp_status sla_slot_table_bytes(int64_t seq, int64_t* packed_bytes, int64_t* flag_bytes);
+
+/* Host-side packing of a (Np x Np) uint8 slot table (SLA_SLOT_NONE = no bias,
+ * other values < n_slots) into the tile layout the kernels read.  Pure CPU:
+ * both outputs are host buffers of the sizes sla_slot_table_bytes returns.
+ * Stands in for the one-hot `fields` tensor of the reference API
+ * (layers/triton_structured_look_attention.py:116-130 loads it per pair).   */
+INTP_API intp_status sla_pack_slot_table(const uint8_t* slots, int64_t patch_count, int32_t n_slots,
+                                uint8_t* packed, uint8_t* tile_flags);
+
+/* Negative L1 distance: out[m,p] = -sum_f |x[m,f] - w[p,f]|, float32, all
+ * row-major contiguous.  Replaces the launch of `_negative_l1_forward` in
+ * `_TritonNegativeL1.forward` (layers/triton_negative_l1.py:157-187), reached
+ * through `negative_l1_distance` (:233-241).                                  */
+INTP_API intp_status nl1_forward(const float* x, const float* w, float* out,
+                        int64_t rows, int64_t protos, int64_t features, void* stream);
+
+/* Copies the device status word written by bounded waits to the host
+ * (synchronous on `stream`) and clears it.  *code = 0 when no wait failed.  */
+INTP_API intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream);
+
+/* Library / device facts: compute capability of the current device and the
+ * library's ABI version.                                                    */
+INTP_API intp_status intp_device_info(int32_t* sm_major, int32_t* sm_minor, int32_t* sm_count);
+INTP_API int32_t intp_abi_version(void);
+INTP_API const char* intp_status_string(intp_status status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INTP_B200_H */

@@ -1,0 +1,128 @@
+"""ctypes binding of ``libintp_b200.so`` (the C ABI in ``include/intp_b200.h``).
+
+The shared library is the only compute path of this package: if it is missing
+or cannot be loaded, every operator raises instead of falling back to CPU or
+PyTorch code.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libintp_b200.so"
+
+INTP_OK = 0
+INTP_ERR_ARGUMENT = 1
+INTP_ERR_SHAPE = 2
+INTP_ERR_DTYPE = 3
+INTP_ERR_LAYOUT = 4
+INTP_ERR_ARCH = 5
+INTP_ERR_LAUNCH = 6
+INTP_ERR_TIMEOUT = 7
+INTP_ERR_UNSUPPORTED = 8
+
+INTP_F32, INTP_F16, INTP_BF16 = 0, 1, 2
+SLA_BIAS_NONE, SLA_BIAS_FIELDS, SLA_BIAS_SLOTS = 0, 1, 2
+SLA_SLOT_NONE = 255
+SLA_KERNEL_AUTO, SLA_KERNEL_SIMT, SLA_KERNEL_TCGEN05 = 0, 1, 2
+
+# Every symbol include/intp_b200.h declares.
+EXPORTED_SYMBOLS = (
+    "sla_forward",
+    "sla_slot_table_bytes",
+    "sla_pack_slot_table",
+    "nl1_forward",
+    "sla_read_status",
+    "intp_device_info",
+    "intp_abi_version",
+    "intp_status_string",
+)
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+_Stride = _i64 * 4
+
+
+class SlaForwardArgs(ctypes.Structure):
+    """Mirror of ``sla_forward_args`` (field order and types must match)."""
+
+    _fields_ = [
+        ("batch", _i64), ("heads", _i64), ("seq", _i64), ("head_dim", _i64),
+        ("scale", ctypes.c_float),
+        ("dtype", _i32),
+        ("q", _vp), ("q_stride", _Stride),
+        ("k", _vp), ("k_stride", _Stride),
+        ("v", _vp), ("v_stride", _Stride),
+        ("out", _vp), ("out_stride", _Stride),
+        ("lse", _vp),
+        ("bias_mode", _i32),
+        ("poses", _i64),
+        ("pose", _vp), ("pose_stride", _Stride), ("pose_dtype", _i32),
+        ("fields", _vp), ("fields_stride", _Stride), ("fields_dtype", _i32),
+        ("slots_packed", _vp),
+        ("slot_tile_flags", _vp),
+        ("dense", _vp), ("dense_stride", _Stride), ("dense_dtype", _i32),
+        ("status", _vp),
+        ("kernel", _i32),
+    ]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class NativeLibraryError(RuntimeError):
+    """The CUDA extension is missing or does not export the expected ABI."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise NativeLibraryError when it is unavailable."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise NativeLibraryError(
+                f"{LIB_PATH} is not built; run `python -m intp_preliminary_b200.build`"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        missing = [name for name in EXPORTED_SYMBOLS if not hasattr(lib, name)]
+        if missing:
+            raise NativeLibraryError(f"{LIB_PATH} lacks symbols {missing}")
+        lib.sla_forward.argtypes = [ctypes.POINTER(SlaForwardArgs), _vp]
+        lib.sla_forward.restype = _i32
+        lib.sla_slot_table_bytes.argtypes = [_i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]
+        lib.sla_slot_table_bytes.restype = _i32
+        lib.sla_pack_slot_table.argtypes = [_vp, _i64, _i32, _vp, _vp]
+        lib.sla_pack_slot_table.restype = _i32
+        lib.nl1_forward.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
+        lib.nl1_forward.restype = _i32
+        lib.sla_read_status.argtypes = [_vp, ctypes.POINTER(_i32), _vp]
+        lib.sla_read_status.restype = _i32
+        lib.intp_device_info.argtypes = [ctypes.POINTER(_i32)] * 3
+        lib.intp_device_info.restype = _i32
+        lib.intp_abi_version.argtypes = []
+        lib.intp_abi_version.restype = _i32
+        lib.intp_status_string.argtypes = [_i32]
+        lib.intp_status_string.restype = ctypes.c_char_p
+        if lib.intp_abi_version() != 1:
+            raise NativeLibraryError("libintp_b200.so ABI version mismatch")
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    return load().intp_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    """Raise the error the reference would raise for a failed launch."""
+    if status == INTP_OK:
+        return
+    message = f"{what}: {status_string(status)} (status {status})"
+    if status in (INTP_ERR_ARGUMENT, INTP_ERR_SHAPE, INTP_ERR_DTYPE, INTP_ERR_LAYOUT):
+        raise ValueError(message)
+    raise RuntimeError(message)

@@ -1,0 +1,202 @@
+// capi.cu - extern "C" boundary of libintp_b200.so (declared in include/intp_b200.h).
+//
+// Validates arguments with the same rules as the reference's Python launch
+// sites, picks the kernel, launches on the caller's stream, and maps every
+// failure to an intp_status.  No exception crosses this boundary and nothing
+// here allocates device memory.
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include "../../include/intp_b200.h"
+#include "sla_internal.h"
+
+namespace {
+
+struct DeviceFacts {
+  int major = 0, minor = 0, sms = 0;
+};
+
+bool device_facts(DeviceFacts* f) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  static std::mutex mu;
+  static DeviceFacts cache[64];
+  static bool have[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && have[dev]) {
+    *f = cache[dev];
+    return true;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return false;
+  f->major = prop.major;
+  f->minor = prop.minor;
+  f->sms = prop.multiProcessorCount;
+  if (dev >= 0 && dev < 64) {
+    cache[dev] = *f;
+    have[dev] = true;
+  }
+  return true;
+}
+
+bool valid_dtype(int32_t d) { return d == INTP_F32 || d == INTP_F16 || d == INTP_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+int32_t intp_abi_version(void) { return 1; }
+
+const char* intp_status_string(intp_status s) {
+  switch (s) {
+    case INTP_OK: return "ok";
+    case INTP_ERR_ARGUMENT: return "invalid argument";
+    case INTP_ERR_SHAPE: return "shape mismatch";
+    case INTP_ERR_DTYPE: return "unsupported dtype";
+    case INTP_ERR_LAYOUT: return "unsupported stride or alignment";
+    case INTP_ERR_ARCH: return "device is not sm_100 (B200)";
+    case INTP_ERR_LAUNCH: return "CUDA launch failure";
+    case INTP_ERR_TIMEOUT: return "a bounded device wait timed out";
+    case INTP_ERR_UNSUPPORTED: return "request outside kernel coverage";
+    default: return "unknown status";
+  }
+}
+
+intp_status intp_device_info(int32_t* sm_major, int32_t* sm_minor, int32_t* sm_count) {
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (sm_major) *sm_major = f.major;
+  if (sm_minor) *sm_minor = f.minor;
+  if (sm_count) *sm_count = f.sms;
+  return INTP_OK;
+}
+
+intp_status sla_slot_table_bytes(int64_t seq, int64_t* packed_bytes, int64_t* flag_bytes) {
+  if (seq < 1 || !packed_bytes || !flag_bytes) return INTP_ERR_ARGUMENT;
+  const int64_t nqt = (seq + intp::kSlotTileQ - 1) / intp::kSlotTileQ;
+  const int64_t nkt = (seq + intp::kSlotTileK - 1) / intp::kSlotTileK;
+  *packed_bytes = nqt * nkt * intp::kSlotTileBytes;
+  *flag_bytes = nqt * nkt;
+  return INTP_OK;
+}
+
+// Packs a patch-indexed (Np x Np) slot table into token-indexed tiles: token i
+// = patch i-1, token 0 (CLS) and padding carry n_slots ("no bias").
+intp_status sla_pack_slot_table(const uint8_t* slots, int64_t patch_count, int32_t n_slots, uint8_t* packed,
+                                uint8_t* tile_flags) {
+  if (!slots || !packed || !tile_flags || patch_count < 0) return INTP_ERR_ARGUMENT;
+  if (n_slots < 1 || n_slots > 254) return INTP_ERR_ARGUMENT;
+  const int64_t seq = patch_count + 1;
+  int64_t pb = 0, fb = 0;
+  sla_slot_table_bytes(seq, &pb, &fb);
+  const int64_t nkt = (seq + intp::kSlotTileK - 1) / intp::kSlotTileK;
+  std::memset(packed, n_slots, static_cast<size_t>(pb));
+  std::memset(tile_flags, 0, static_cast<size_t>(fb));
+  for (int64_t pq = 0; pq < patch_count; ++pq) {
+    const int64_t i = pq + 1;
+    const int64_t qt = i / intp::kSlotTileQ, r = i % intp::kSlotTileQ;
+    for (int64_t pk = 0; pk < patch_count; ++pk) {
+      const uint8_t s = slots[pq * patch_count + pk];
+      if (s == SLA_SLOT_NONE) continue;
+      if (s >= n_slots) return INTP_ERR_ARGUMENT;
+      const int64_t j = pk + 1;
+      const int64_t kt = j / intp::kSlotTileK, c = j % intp::kSlotTileK;
+      const int64_t off = (qt * nkt + kt) * intp::kSlotTileBytes + (c / 16) * 2048 + r * 16 + (c % 16);
+      packed[off] = s;
+      tile_flags[qt * nkt + kt] = 1;
+    }
+  }
+  return INTP_OK;
+}
+
+intp_status sla_forward(const sla_forward_args* a, void* stream) {
+  if (!a) return INTP_ERR_ARGUMENT;
+  if (a->batch < 0 || a->heads < 0 || a->seq < 1 || a->head_dim < 1) return INTP_ERR_SHAPE;
+  if (!valid_dtype(a->dtype)) return INTP_ERR_DTYPE;
+  if (a->batch == 0 || a->heads == 0) return INTP_OK;
+  if (!a->q || !a->k || !a->v || !a->out) return INTP_ERR_ARGUMENT;
+  if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 || a->out_stride[3] != 1)
+    return INTP_ERR_LAYOUT;
+  if (a->bias_mode == SLA_BIAS_FIELDS) {
+    if (!a->pose || !a->fields || a->poses < 1) return INTP_ERR_ARGUMENT;
+    if (!valid_dtype(a->pose_dtype) || !valid_dtype(a->fields_dtype)) return INTP_ERR_DTYPE;
+  } else if (a->bias_mode == SLA_BIAS_SLOTS) {
+    if (!a->pose || !a->slots_packed || !a->slot_tile_flags || a->poses < 1 || a->poses > 254)
+      return INTP_ERR_ARGUMENT;
+    if (!valid_dtype(a->pose_dtype)) return INTP_ERR_DTYPE;
+  } else if (a->bias_mode != SLA_BIAS_NONE) {
+    return INTP_ERR_ARGUMENT;
+  }
+  if (a->dense && !valid_dtype(a->dense_dtype)) return INTP_ERR_DTYPE;
+  if (a->kernel < SLA_KERNEL_AUTO || a->kernel > SLA_KERNEL_TCGEN05) return INTP_ERR_ARGUMENT;
+
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (f.major != 10) return INTP_ERR_ARCH;
+
+  intp::SlaParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.batch = a->batch;
+  p.heads = a->heads;
+  p.seq = a->seq;
+  p.head_dim = a->head_dim;
+  p.scale = a->scale;
+  p.dtype = a->dtype;
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.out = a->out;
+  std::memcpy(p.q_stride, a->q_stride, sizeof(p.q_stride));
+  std::memcpy(p.k_stride, a->k_stride, sizeof(p.k_stride));
+  std::memcpy(p.v_stride, a->v_stride, sizeof(p.v_stride));
+  std::memcpy(p.out_stride, a->out_stride, sizeof(p.out_stride));
+  p.lse = a->lse;
+  p.bias_mode = a->bias_mode;
+  p.poses = a->poses;
+  p.pose = a->pose;
+  std::memcpy(p.pose_stride, a->pose_stride, sizeof(p.pose_stride));
+  p.pose_dtype = a->pose_dtype;
+  p.fields = a->fields;
+  std::memcpy(p.fields_stride, a->fields_stride, sizeof(p.fields_stride));
+  p.fields_dtype = a->fields_dtype;
+  p.slots_packed = a->slots_packed;
+  p.slot_tile_flags = a->slot_tile_flags;
+  p.dense = a->dense;
+  std::memcpy(p.dense_stride, a->dense_stride, sizeof(p.dense_stride));
+  p.dense_dtype = a->dense_dtype;
+  p.status = a->status;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->kernel != SLA_KERNEL_SIMT && intp::sla_tc_supported(p)) return intp::launch_sla_tc(p, s, f.sms);
+  if (a->kernel == SLA_KERNEL_TCGEN05) return INTP_ERR_UNSUPPORTED;
+  return intp::launch_sla_simt(p, s);
+}
+
+intp_status nl1_forward(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
+                        void* stream) {
+  if (rows < 0 || protos < 0 || features < 0) return INTP_ERR_SHAPE;
+  if (rows == 0 || protos == 0) return INTP_OK;
+  if (!x || !w || !out) return INTP_ERR_ARGUMENT;
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (f.major != 10) return INTP_ERR_ARCH;
+  return intp::launch_nl1(x, w, out, rows, protos, features, static_cast<cudaStream_t>(stream));
+}
+
+intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream) {
+  if (!status_dev || !code) return INTP_ERR_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t host = 0;
+  if (cudaMemcpyAsync(&host, status_dev, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return INTP_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return INTP_ERR_LAUNCH;
+  *code = host;
+  if (host != 0) {
+    if (cudaMemsetAsync(status_dev, 0, sizeof(int32_t), s) != cudaSuccess) return INTP_ERR_LAUNCH;
+    return INTP_ERR_TIMEOUT;
+  }
+  return INTP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,43 @@
+// sla_internal.h - kernel-side parameter block shared by the Look-attention
+// kernels and the C-ABI dispatcher (capi.cu).  Not part of the public ABI.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace intp {
+
+struct SlaParams {
+  int64_t batch, heads, seq, head_dim;
+  float scale;
+  int32_t dtype;
+  const void* q; int64_t q_stride[4];
+  const void* k; int64_t k_stride[4];
+  const void* v; int64_t v_stride[4];
+  void* out; int64_t out_stride[4];
+  float* lse;
+  int32_t bias_mode;
+  int64_t poses;
+  const void* pose; int64_t pose_stride[4]; int32_t pose_dtype;
+  const void* fields; int64_t fields_stride[4]; int32_t fields_dtype;
+  const uint8_t* slots_packed;
+  const uint8_t* slot_tile_flags;
+  const void* dense; int64_t dense_stride[4]; int32_t dense_dtype;
+  int32_t* status;
+};
+
+// Packed slot-table geometry (shared by the host packer and both kernels):
+// tiles of 128 query tokens x 64 key tokens, 8192 bytes each, stored
+// [q_tile][k_tile][key_chunk(4)][query(128)][16 keys].  Entry = slot index,
+// or n_slots for "no Look bias" (CLS row/column, padding, unslotted pairs).
+constexpr int kSlotTileQ = 128;
+constexpr int kSlotTileK = 64;
+constexpr int kSlotTileBytes = kSlotTileQ * kSlotTileK;
+
+int32_t launch_sla_simt(const SlaParams& p, cudaStream_t stream);
+// Returns INTP_ERR_UNSUPPORTED (8) when the tensor-core path does not apply.
+int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count);
+int32_t sla_tc_supported(const SlaParams& p);
+int32_t launch_nl1(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
+                   cudaStream_t stream);
+
+}  // namespace intp

@@ -1,0 +1,275 @@
+"""Structured Look attention on B200: the drop-in for
+``layers/triton_structured_look_attention.py`` of the reference.
+
+``structured_look_attention(q, k, v, pose, fields, *, scale, dense_bias=None)``
+keeps the reference signature and result (layers/triton_structured_look_attention.py:412-424):
+
+    S = scale * q @ k^T                         (B, H, N, N), fp32
+    S[:, :, 1:, 1:] += einsum("bqhp,hpqk->bhqk", pose, fields) (+ dense_bias)
+    out = softmax(S, -1) @ v                    cast to q.dtype
+
+with ``q/k/v`` of shape ``(B, H, N, D)`` (token 0 is CLS, N = Np + 1), ``pose``
+``(B, Np, H, P)`` and ``fields`` ``(H, P, Np, Np)``.
+
+``fields`` may also be a :class:`LookSlots`, the compact form of one-hot fields
+(``fields[h, p, q, k] = 1[slot(q, k) == p]``): the per-pair slot table is
+shared by every batch and head and the bias becomes ``pose[b, q, h, slot]``.
+That is the form the tensor-core kernel consumes without ever materialising an
+``Np x Np`` bias or field tensor.
+
+Every call runs the CUDA kernels of ``libintp_b200.so``; there is no CPU or
+PyTorch fallback.  CPU tensors raise ``ValueError`` like any other input the
+kernels cannot take.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.INTP_F32, torch.float16: _lib.INTP_F16, torch.bfloat16: _lib.INTP_BF16}
+_KERNELS = {"auto": _lib.SLA_KERNEL_AUTO, "simt": _lib.SLA_KERNEL_SIMT, "tcgen05": _lib.SLA_KERNEL_TCGEN05}
+
+
+class LookSlots:
+    """Pair table standing in for one-hot Look fields of shape ``(H, P, Np, Np)``.
+
+    ``slots`` is an ``(Np, Np)`` uint8 array/tensor: ``slots[q, k]`` is the
+    index ``p < n_slots`` of the query's Look field that pair ``(q, k)`` reads,
+    or 255 for "no bias".  The packed tile layout the kernels read is built
+    once on the host (``sla_pack_slot_table``) and cached per device.
+    """
+
+    def __init__(self, slots, n_slots: int, heads: int | None = None) -> None:
+        table = slots.detach().cpu().numpy() if isinstance(slots, torch.Tensor) else np.asarray(slots)
+        if table.ndim != 2 or table.shape[0] != table.shape[1]:
+            raise ValueError("slots must be a square (Np, Np) table")
+        if not 1 <= int(n_slots) <= 254:
+            raise ValueError("n_slots must be in [1, 254]")
+        table = np.ascontiguousarray(table.astype(np.uint8))
+        used = table[table != _lib.SLA_SLOT_NONE]
+        if used.size and int(used.max()) >= int(n_slots):
+            raise ValueError("slot index out of range for n_slots")
+        self.table = table
+        self.n_slots = int(n_slots)
+        self.heads = heads
+        self._packed: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        self._host: tuple[np.ndarray, np.ndarray] | None = None
+        self._lock = threading.Lock()
+
+    @property
+    def patch_count(self) -> int:
+        return int(self.table.shape[0])
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        heads = -1 if self.heads is None else self.heads
+        return (heads, self.n_slots, self.patch_count, self.patch_count)
+
+    def host_packed(self) -> tuple[np.ndarray, np.ndarray]:
+        """Packed tiles and per-tile flags as host arrays (pure CPU)."""
+        if self._host is None:
+            lib = _lib.load()
+            seq = self.patch_count + 1
+            pb, fb = ctypes.c_int64(), ctypes.c_int64()
+            _lib.check(lib.sla_slot_table_bytes(seq, ctypes.byref(pb), ctypes.byref(fb)), "sla_slot_table_bytes")
+            packed = np.empty(pb.value, dtype=np.uint8)
+            flags = np.empty(fb.value, dtype=np.uint8)
+            _lib.check(
+                lib.sla_pack_slot_table(
+                    self.table.ctypes.data, self.patch_count, self.n_slots, packed.ctypes.data, flags.ctypes.data
+                ),
+                "sla_pack_slot_table",
+            )
+            self._host = (packed, flags)
+        return self._host
+
+    def device_packed(self, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+        index = torch.device(device).index
+        with self._lock:
+            if index not in self._packed:
+                packed, flags = self.host_packed()
+                self._packed[index] = (
+                    torch.from_numpy(packed).to(device),
+                    torch.from_numpy(flags).to(device),
+                )
+            return self._packed[index]
+
+    def dense_fields(self, heads: int, *, dtype=torch.float32, device=None) -> torch.Tensor:
+        """Materialise the equivalent one-hot ``(H, P, Np, Np)`` fields (for checks)."""
+        table = torch.from_numpy(self.table.astype(np.int64))
+        onehot = torch.zeros(self.n_slots + 1, self.patch_count, self.patch_count, dtype=dtype)
+        index = torch.where(table == _lib.SLA_SLOT_NONE, torch.full_like(table, self.n_slots), table)
+        onehot.scatter_(0, index.unsqueeze(0), 1.0)
+        fields = onehot[: self.n_slots].unsqueeze(0).expand(heads, -1, -1, -1).contiguous()
+        return fields if device is None else fields.to(device)
+
+
+_status_words: dict[int, torch.Tensor] = {}
+_status_lock = threading.Lock()
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    index = torch.device(device).index
+    with _status_lock:
+        word = _status_words.get(index)
+        if word is None:
+            word = torch.zeros(1, dtype=torch.int32, device=device)
+            _status_words[index] = word
+        return word
+
+
+def check_device_status(device=None) -> None:
+    """Synchronise and raise if a bounded device wait gave up since the last check."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    word = _status_word(device)
+    code = ctypes.c_int32()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        status = _lib.load().sla_read_status(ctypes.c_void_p(word.data_ptr()), ctypes.byref(code), ctypes.c_void_p(stream))
+    if status != _lib.INTP_OK:
+        raise RuntimeError(f"device wait failed: code {code.value:#x} ({_lib.status_string(status)})")
+
+
+def _stride4(t: torch.Tensor):
+    return _lib._Stride(*[int(s) for s in t.stride()])
+
+
+def _validate(q, k, v, pose, fields, dense_bias):
+    """The reference's checks, in its order (layers/triton_structured_look_attention.py:298-319)."""
+    tensors = [q, k, v, pose] + ([fields] if isinstance(fields, torch.Tensor) else [])
+    if dense_bias is not None:
+        tensors.append(dense_bias)
+    if not all(isinstance(t, torch.Tensor) and t.is_cuda for t in tensors):
+        raise ValueError("structured Look attention requires CUDA tensors")
+    if q.shape != k.shape or q.shape != v.shape or q.ndim != 4:
+        raise ValueError("q, k, and v must share shape (B,H,N,D)")
+    if pose.ndim != 4 or len(fields.shape) != 4:
+        raise ValueError("pose and fields must have shapes (B,N,H,P) and (H,P,N,N)")
+    batch, heads, sequence, head_dim = q.shape
+    patch_count, poses = pose.shape[1], pose.shape[-1]
+    if pose.shape != (batch, patch_count, heads, poses):
+        raise ValueError("pose shape is inconsistent with q")
+    if isinstance(fields, LookSlots):
+        if fields.n_slots != poses or fields.patch_count != patch_count or fields.heads not in (None, heads):
+            raise ValueError("fields shape is inconsistent with pose")
+    elif fields.shape != (heads, poses, patch_count, patch_count):
+        raise ValueError("fields shape is inconsistent with pose")
+    if dense_bias is not None and dense_bias.shape != (batch, heads, patch_count, patch_count):
+        raise ValueError("dense_bias shape is inconsistent with q")
+    if sequence != patch_count + 1:
+        raise ValueError("sequence must be patch_count + one CLS token")
+    if head_dim > 128:
+        raise ValueError("head_dim above 128 is not supported")
+    devices = {t.device for t in tensors}
+    if len(devices) != 1:
+        raise ValueError("all tensors must be on the same CUDA device")
+    for t in (q, k, v):
+        if t.dtype not in _DTYPE_CODE:
+            raise ValueError("q, k, v must be float32, float16 or bfloat16")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k and v must share a dtype")
+
+
+def look_attention_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    pose: torch.Tensor,
+    fields,
+    *,
+    scale: float,
+    dense_bias: torch.Tensor | None = None,
+    want_lse: bool = False,
+    kernel: str = "auto",
+    out: torch.Tensor | None = None,
+):
+    """Forward only.  Returns ``(out, lse_or_None)``.
+
+    ``kernel`` selects the implementation: ``"auto"`` (tensor cores when the
+    inputs qualify, else CUDA cores), ``"simt"`` or ``"tcgen05"`` (raises if
+    the tensor-core path cannot take the inputs).
+    """
+    _validate(q, k, v, pose, fields, dense_bias)
+    batch, heads, sequence, head_dim = q.shape
+    device = q.device
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError("q, k, v need a unit stride on head_dim")
+    if out is None:
+        out = torch.empty((batch, heads, sequence, head_dim), dtype=q.dtype, device=device)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.device != device or out.stride(-1) != 1:
+        raise ValueError("out must match q in shape, dtype and device with unit stride on head_dim")
+    lse = torch.empty((batch, heads, sequence), dtype=torch.float32, device=device) if want_lse else None
+
+    args = _lib.SlaForwardArgs()
+    args.batch, args.heads, args.seq, args.head_dim = batch, heads, sequence, head_dim
+    args.scale = float(scale)
+    args.dtype = _DTYPE_CODE[q.dtype]
+    args.q, args.q_stride = q.data_ptr(), _stride4(q)
+    args.k, args.k_stride = k.data_ptr(), _stride4(k)
+    args.v, args.v_stride = v.data_ptr(), _stride4(v)
+    args.out, args.out_stride = out.data_ptr(), _stride4(out)
+    args.lse = lse.data_ptr() if lse is not None else None
+    keep = []
+    pose_f = pose if pose.dtype in _DTYPE_CODE else pose.float()
+    keep.append(pose_f)
+    args.poses = pose_f.shape[-1]
+    args.pose, args.pose_stride, args.pose_dtype = pose_f.data_ptr(), _stride4(pose_f), _DTYPE_CODE[pose_f.dtype]
+    if isinstance(fields, LookSlots):
+        packed, flags = fields.device_packed(device)
+        args.bias_mode = _lib.SLA_BIAS_SLOTS
+        args.slots_packed, args.slot_tile_flags = packed.data_ptr(), flags.data_ptr()
+    else:
+        fields_f = fields if fields.dtype in _DTYPE_CODE else fields.float()
+        keep.append(fields_f)
+        args.bias_mode = _lib.SLA_BIAS_FIELDS
+        args.fields, args.fields_stride = fields_f.data_ptr(), _stride4(fields_f)
+        args.fields_dtype = _DTYPE_CODE[fields_f.dtype]
+    if dense_bias is not None:
+        dense_f = dense_bias if dense_bias.dtype in _DTYPE_CODE else dense_bias.float()
+        keep.append(dense_f)
+        args.dense, args.dense_stride, args.dense_dtype = dense_f.data_ptr(), _stride4(dense_f), _DTYPE_CODE[dense_f.dtype]
+    args.status = _status_word(device).data_ptr()
+    if kernel not in _KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
+    args.kernel = _KERNELS[kernel]
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        status = lib.sla_forward(ctypes.byref(args), ctypes.c_void_p(stream))
+    _lib.check(status, "structured Look attention")
+    return out, lse
+
+
+class _StructuredLookAttention(torch.autograd.Function):
+    """Autograd wrapper; the forward is the CUDA kernel, the backward is not built yet."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, pose, fields, dense_bias, scale):
+        out, _ = look_attention_forward(
+            q, k, v, pose, fields, scale=scale, dense_bias=dense_bias if dense_bias.numel() else None
+        )
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        raise NotImplementedError(
+            "structured Look attention backward is not implemented on this build (forward/inference only)"
+        )
+
+
+def structured_look_attention(q, k, v, pose, fields, *, scale, dense_bias=None):
+    """Memory-bounded Look attention forward (layers/triton_structured_look_attention.py:412-424)."""
+    if not torch.is_grad_enabled() or not any(
+        t.requires_grad for t in (q, k, v, pose, fields, dense_bias) if isinstance(t, torch.Tensor)
+    ):
+        out, _ = look_attention_forward(q, k, v, pose, fields, scale=scale, dense_bias=dense_bias)
+        return out
+    if dense_bias is None:
+        dense_bias = q.new_empty(0)
+    return _StructuredLookAttention.apply(q, k, v, pose, fields, dense_bias, float(scale))

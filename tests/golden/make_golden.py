@@ -1,0 +1,149 @@
+"""Generate the golden fixtures of tests/golden/ by running the REFERENCE code.
+
+This script imports the reference's own Python modules (it must run where the
+reference checkout is available, passed as --reference, default
+/root/reference) and records their outputs on seeded inputs:
+
+  look_attention_reference.npz
+      ``reference_structured_look_attention`` (layers/triton_structured_look_attention.py:25-54)
+      on the reference test's inputs (tests/test_triton_structured_look_attention.py:10-20,
+      seed 17, P = 8 and 18, with and without dense bias), and on synthetic
+      Look configurations (14x14 lattice, 12 directions x 4 rings, fp32;
+      32x32 lattice, 8 directions x 4 rings, bf16 inputs) expressed through
+      one-hot fields.
+  negative_l1_reference.npz
+      ``negative_l1_distance`` CPU path (layers/triton_negative_l1.py:233-241) on the
+      reference test shapes and a small slice of the BASELINE shapes.
+  hex_bins_reference.npz
+      ``hex_relative_bins`` (utils/hex_graph.py:25-47) on the synthetic
+      14x14 lattice and on the real half6d3r tokenizer lattice (195 patches).
+
+The slot tables of the synthetic configurations come from the scalar oracle
+restatement (oracle/hex_lattice.py); the reference has no code for that
+binning (it is defined by the benchmark description), so the fixture pins the
+reference's attention math on those inputs and the product's table builder is
+checked against the oracle separately.
+
+Run: python tests/golden/make_golden.py [--reference PATH]
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+
+
+def _synthetic_case(ref_fn, lattice, *, rows, cols, n_dir, n_rad, batch, heads, dim, dtype, seed):
+    points = lattice.lattice_points(rows, cols)
+    slots = np.asarray(lattice.slot_table(points, n_dir, n_rad), dtype=np.uint8)
+    patches = rows * cols
+    n_slots = n_dir * n_rad
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(batch, heads, patches + 1, dim, generator=g) / 8).to(dtype)
+    k = (torch.randn(batch, heads, patches + 1, dim, generator=g) / 8).to(dtype)
+    v = (torch.randn(batch, heads, patches + 1, dim, generator=g) / 8).to(dtype)
+    pose = torch.rand(batch, patches, heads, n_slots, generator=g) * 2 - 1
+    onehot = torch.zeros(n_slots, patches, patches)
+    table = torch.from_numpy(slots.astype(np.int64))
+    for p in range(n_slots):
+        onehot[p] = (table == p).float()
+    fields = onehot.unsqueeze(0).expand(heads, -1, -1, -1)
+    out = ref_fn(q, k, v, pose, fields, scale=1 / math.sqrt(dim))
+    def raw(t):
+        # bf16 inputs are stored as their 16-bit patterns to halve the fixture size
+        return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+    return {
+        "q": raw(q), "k": raw(k), "v": raw(v),
+        "pose": pose.numpy(), "slots": slots, "out": out.float().numpy(),
+        "scale": np.float64(1 / math.sqrt(dim)), "n_slots": np.int64(n_slots),
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--reference", default="/root/reference")
+    args = parser.parse_args()
+    sys.path.insert(0, str(Path(args.reference).resolve()))
+    sys.path.insert(0, str(REPO))
+    from layers.triton_structured_look_attention import reference_structured_look_attention as ref_attn
+    from layers.triton_negative_l1 import negative_l1_distance as ref_nl1
+    from utils.hex_graph import hex_relative_bins
+    from oracle import hex_lattice
+
+    # --- structured Look attention ------------------------------------------------
+    look = {}
+    for poses in (8, 18):
+        torch.manual_seed(17)  # tests/test_triton_structured_look_attention.py:10-20
+        batch, heads, patches, dim = 2, 3, 7, 16
+        tensors = [torch.randn(batch, heads, patches + 1, dim) for _ in range(3)]
+        tensors.append(torch.randn(batch, patches, heads, poses))
+        tensors.append(torch.randn(heads, poses, patches, patches))
+        dense = torch.randn(2, 3, 7, 7)
+        scale = 1 / 16 ** 0.5
+        out = ref_attn(*tensors, scale=scale)
+        out_dense = ref_attn(*tensors, scale=scale, dense_bias=dense)
+        for name, t in zip(("q", "k", "v", "pose", "fields"), tensors):
+            look[f"p{poses}_{name}"] = t.numpy()
+        look[f"p{poses}_dense"] = dense.numpy()
+        look[f"p{poses}_out"] = out.numpy()
+        look[f"p{poses}_out_dense"] = out_dense.numpy()
+        look[f"p{poses}_scale"] = np.float64(scale)
+        half = [t.half() for t in tensors]
+        look[f"p{poses}_out_half"] = ref_attn(*half, scale=scale).float().numpy()
+    cfg1 = _synthetic_case(ref_attn, hex_lattice, rows=14, cols=14, n_dir=12, n_rad=4,
+                           batch=1, heads=3, dim=64, dtype=torch.float32, seed=1)
+    for key, value in cfg1.items():
+        look[f"cfg1_{key}"] = value
+    cfg4 = _synthetic_case(ref_attn, hex_lattice, rows=32, cols=32, n_dir=8, n_rad=4,
+                           batch=1, heads=1, dim=64, dtype=torch.bfloat16, seed=4)
+    for key, value in cfg4.items():
+        look[f"cfg4_{key}"] = value
+    np.savez_compressed(HERE / "look_attention_reference.npz", **look)
+
+    # --- negative L1 ----------------------------------------------------------------
+    nl1 = {}
+    g = torch.Generator().manual_seed(3)
+    for name, (m, p, f) in {"t7x11": (7, 5, 11), "t37x67": (37, 13, 67), "b432": (24, 40, 432),
+                            "b1728": (8, 24, 1728)}.items():
+        x = torch.randn(m, f, generator=g)
+        w = torch.randn(p, f, generator=g) * 0.5
+        nl1[f"{name}_x"] = x.numpy()
+        nl1[f"{name}_w"] = w.numpy()
+        nl1[f"{name}_out"] = ref_nl1(x, w).numpy()
+    np.savez_compressed(HERE / "negative_l1_reference.npz", **nl1)
+
+    # --- hex geometry ---------------------------------------------------------------
+    hexes = {}
+    points = torch.tensor(hex_lattice.lattice_points(14, 14), dtype=torch.float64)
+    rings, dirs = hex_relative_bins(points)
+    hexes["lattice14_xy"] = points.numpy()
+    hexes["lattice14_rings"] = rings.numpy().astype(np.uint8)
+    hexes["lattice14_dirs"] = dirs.numpy().astype(np.uint8)
+    from layers.hex_rotating_harmonic_patch_embed import HexRotatingHarmonicPatchEmbed
+    embed = HexRotatingHarmonicPatchEmbed(
+        img_size=224, in_chans=3, embed_dim=192, lattice_stride=18, kernel_sizes=(24, 12), bases=96,
+        directions=6, global_directions=12, angular_bins_per_radius=3, prototype_chunk_size=16,
+        null_initial_score=0.0, pose_softmax=True, use_null=True, match_metric="dot",
+    )
+    coo = embed.coo_patchs
+    real_xy = torch.stack((coo.real, coo.imag), dim=-1)
+    rings, dirs = hex_relative_bins(real_xy)
+    hexes["real_xy"] = real_xy.numpy()
+    hexes["real_rings"] = rings.numpy().astype(np.uint8)
+    hexes["real_dirs"] = dirs.numpy().astype(np.uint8)
+    np.savez_compressed(HERE / "hex_bins_reference.npz", **hexes)
+    for path in sorted(HERE.glob("*.npz")):
+        print(path.name, path.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,106 @@
+"""The C-ABI library loads, exports every declared symbol and its host-only
+functions behave (no GPU needed: nothing here launches a kernel)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from intp_preliminary_b200 import _lib
+from intp_preliminary_b200.look_attention import LookSlots
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "intp_b200.h"
+
+
+def _declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"INTP_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.load()
+    declared = _declared_functions()
+    assert declared, "no declarations found"
+    assert set(declared) == set(_lib.EXPORTED_SYMBOLS)
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.intp_abi_version() == 1
+    assert _lib.status_string(_lib.INTP_OK) == "ok"
+    assert "timed out" in _lib.status_string(_lib.INTP_ERR_TIMEOUT)
+
+
+def test_struct_layout_matches_header_field_order():
+    text = HEADER.read_text()
+    body = text[text.index("typedef struct sla_forward_args"):text.index("} sla_forward_args;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = re.findall(r"(\w+)(?:\[4\])?\s*[;,]", body)
+    ctypes_names = [f[0] for f in _lib.SlaForwardArgs._fields_]
+    assert names == ctypes_names
+
+
+def test_slot_table_bytes():
+    lib = _lib.load()
+    pb, fb = ctypes.c_int64(), ctypes.c_int64()
+    assert lib.sla_slot_table_bytes(197, ctypes.byref(pb), ctypes.byref(fb)) == 0
+    assert pb.value == 2 * 4 * 8192 and fb.value == 8
+    assert lib.sla_slot_table_bytes(0, ctypes.byref(pb), ctypes.byref(fb)) == _lib.INTP_ERR_ARGUMENT
+
+
+def test_pack_slot_table_layout():
+    rng = np.random.default_rng(0)
+    patches = 150
+    table = rng.integers(0, 20, size=(patches, patches)).astype(np.uint8)
+    table[rng.random((patches, patches)) < 0.5] = 255
+    packed, flags = LookSlots(table, 20).host_packed()
+    seq = patches + 1
+    nkt = (seq + 63) // 64
+    for i in range(seq):
+        for j in range(0, seq, 7):
+            qt, r = divmod(i, 128)
+            kt, c = divmod(j, 64)
+            value = packed[(qt * nkt + kt) * 8192 + (c // 16) * 2048 + r * 16 + c % 16]
+            if i == 0 or j == 0 or table[i - 1, j - 1] == 255:
+                assert value == 20
+            else:
+                assert value == table[i - 1, j - 1]
+    assert flags.sum() > 0
+
+
+def test_pack_rejects_out_of_range_slot():
+    table = np.full((4, 4), 255, np.uint8)
+    table[1, 2] = 7
+    with pytest.raises(ValueError):
+        LookSlots(table, 5)
+
+
+def test_forward_rejects_bad_arguments_without_launching():
+    lib = _lib.load()
+    args = _lib.SlaForwardArgs()
+    args.batch, args.heads, args.seq, args.head_dim = 1, 1, 0, 64
+    assert lib.sla_forward(ctypes.byref(args), None) == _lib.INTP_ERR_SHAPE
+    args.seq, args.dtype = 8, 9
+    assert lib.sla_forward(ctypes.byref(args), None) == _lib.INTP_ERR_DTYPE
+    args.dtype = _lib.INTP_BF16
+    assert lib.sla_forward(ctypes.byref(args), None) == _lib.INTP_ERR_ARGUMENT  # null pointers
+    assert lib.sla_forward(None, None) == _lib.INTP_ERR_ARGUMENT
+    assert lib.nl1_forward(None, None, None, -1, 1, 1, None) == _lib.INTP_ERR_SHAPE
+
+
+def test_operators_refuse_cpu_tensors():
+    import torch
+
+    from intp_preliminary_b200 import negative_l1_distance, structured_look_attention
+
+    q = torch.randn(1, 1, 3, 16)
+    with pytest.raises(ValueError, match="CUDA"):
+        structured_look_attention(q, q, q, torch.randn(1, 2, 1, 4), torch.randn(1, 4, 2, 2), scale=0.25)
+    with pytest.raises(ValueError, match="CUDA"):
+        negative_l1_distance(torch.randn(3, 4), torch.randn(2, 4))
+    with pytest.raises(ValueError, match="feature"):
+        negative_l1_distance(torch.randn(3, 4), torch.randn(2, 5))
