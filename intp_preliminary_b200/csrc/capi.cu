@@ -177,7 +177,7 @@ intp_status nl1_forward(const float* x, const float* w, float* out, int64_t rows
                         void* stream) {
   if (rows < 0 || protos < 0 || features < 0) return INTP_ERR_SHAPE;
   if (rows == 0 || protos == 0) return INTP_OK;
-  if (!x || !w || !out) return INTP_ERR_ARGUMENT;
+  if (!out || (features > 0 && (!x || !w))) return INTP_ERR_ARGUMENT;
   DeviceFacts f;
   if (!device_facts(&f)) return INTP_ERR_LAUNCH;
   if (f.major != 10) return INTP_ERR_ARCH;

@@ -84,12 +84,35 @@ __device__ __forceinline__ int32_t map_coord(const MapOrder& o, int pos, int32_t
   return o.row == pos ? row : (o.head == pos ? head : batch);
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Row maximum of 64 values as a shallow tree of three-input maxima.
+__device__ __forceinline__ float row_max64(const float (&t)[64]) {
+  float m8[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float* v = t + 8 * k;
+    m8[k] = fmaxf(fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]), v[6]), v[7]);
+  }
+  return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+}
+
+__device__ __forceinline__ uint32_t pack_out(uint32_t lo, uint32_t hi, float inv, int32_t dtype) {
+  const float a = __uint_as_float(lo) * inv, b = __uint_as_float(hi) * inv;
+  return dtype == 2 ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+}
+
 struct TcArgs {
   SlaParams p;
   MapOrder oq, ok, ov;
   int64_t n_qt, n_kt, n_items;
   int32_t n_slots;        // 0 when there is no Look bias
   uint32_t table_bytes;   // bytes of the per-query Look table in smem
+  int32_t pose_vec4;      // pose rows are 16-byte aligned fp32 with unit slot stride
 };
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -276,7 +299,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     // ------------------------------------------------------------ softmax warpgroup
     const int row = threadIdx.x;  // 0..127, TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const float scale_log2 = p.scale * kLog2e;
+    const float scale_log2 = p.scale * kLog2e;  // > 0 (checked on the host)
     const int32_t ns = a.n_slots;
     uint32_t s_iter = 0, kv_iter = 0, pv_iter = 0;
     bool ok = true;
@@ -286,16 +309,37 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       const int64_t h = bh % H, b = bh / H;
       const int64_t i = qt * BM + row;  // token index of this thread's row
       if (use_bias) {
-        // Per-query Look values, [slot][row] layout (bank = row % 32: conflict free),
-        // pre-scaled to the log2 domain.  Only this thread reads its column.
+        // Per-query Look values, [slot][row] layout (bank = row % 32: conflict
+        // free), pre-scaled to the log2 domain.  Only this thread reads its column.
         const bool valid = i >= 1 && i < N;
         const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
-        for (int s = 0; s < ns; ++s)
-          table_s[s * BM + row] = valid ? load_any(p.pose, base + s * p.pose_stride[3], p.pose_dtype) * kLog2e : 0.f;
+        if (a.pose_vec4) {
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
+          for (int s4 = 0; s4 < ns / 4; ++s4) {
+            const float4 v4 = valid ? __ldg(src + s4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            table_s[(4 * s4 + 0) * BM + row] = v4.x * kLog2e;
+            table_s[(4 * s4 + 1) * BM + row] = v4.y * kLog2e;
+            table_s[(4 * s4 + 2) * BM + row] = v4.z * kLog2e;
+            table_s[(4 * s4 + 3) * BM + row] = v4.w * kLog2e;
+          }
+        } else {
+          for (int s = 0; s < ns; ++s)
+            table_s[s * BM + row] =
+                valid ? load_any(p.pose, base + s * p.pose_stride[3], p.pose_dtype) * kLog2e : 0.f;
+        }
         table_s[ns * BM + row] = 0.f;
       }
       float m = -INFINITY, l = 0.f;
+      uint64_t tile_mask = 0;  // bit k: key tile (j & ~63) + k carries Look bias
       for (int64_t j = 0; j < n_kt; ++j, ++kv_iter) {
+        if (use_bias && (j & 63) == 0) {
+          // Each warp gathers the flags of the next 64 key tiles with one ballot pair.
+          const int64_t t0 = j + lane, t1 = j + 32 + lane;
+          const bool f0 = t0 < n_kt && p.slot_tile_flags[qt * n_kt + t0] != 0;
+          const bool f1 = t1 < n_kt && p.slot_tile_flags[qt * n_kt + t1] != 0;
+          tile_mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, f0)) |
+                      (static_cast<uint64_t>(__ballot_sync(0xffffffffu, f1)) << 32);
+        }
         const uint32_t sb = s_iter & 1;
         if (!mbar_wait(&bars->s_full[sb], (s_iter >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
           ok = false;
@@ -317,10 +361,10 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           reg_fence16(r3);
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            t[e] = __uint_as_float(r0[e]) * scale_log2;
-            t[16 + e] = __uint_as_float(r1[e]) * scale_log2;
-            t[32 + e] = __uint_as_float(r2[e]) * scale_log2;
-            t[48 + e] = __uint_as_float(r3[e]) * scale_log2;
+            t[e] = __uint_as_float(r0[e]);
+            t[16 + e] = __uint_as_float(r1[e]);
+            t[32 + e] = __uint_as_float(r2[e]);
+            t[48 + e] = __uint_as_float(r3[e]);
           }
         }
         tc_fence_before();
@@ -328,22 +372,25 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         if (lane == 0) mbar_arrive(&bars->s_free[sb]);
         ++s_iter;
 
+        // t holds raw scores on tiles without Look bias, and the log2-domain
+        // logits scale*log2(e)*s + bias on tiles with it.
         const uint32_t st = kv_iter % kStages;
-        const bool bias_tile = use_bias && p.slot_tile_flags[qt * n_kt + j];
+        const bool bias_tile = (tile_mask >> (j & 63)) & 1u;
         if (bias_tile) {
           if (!mbar_wait(&bars->kv_full[st], (kv_iter / kStages) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
             ok = false;
             break;
           }
           const uint8_t* srow = slot_s + st * kSlotBytes + row * 16;
+          const float* trow = table_s + row;
 #pragma unroll
           for (int c = 0; c < BN / 16; ++c) {
             const uint4 w = *reinterpret_cast<const uint4*>(srow + c * 2048);
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const uint32_t slot = (ww[e >> 2] >> ((e & 3) * 8)) & 0xFFu;
-              t[c * 16 + e] += table_s[slot * BM + row];
+              const uint32_t slot = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
+              t[c * 16 + e] = fmaf(t[c * 16 + e], scale_log2, trow[slot * BM]);
             }
           }
         }
@@ -356,9 +403,8 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           for (int c = 0; c < BN; ++c)
             if (key0 + c >= N) t[c] = -INFINITY;
         }
-        float mx = t[0];
-#pragma unroll
-        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, t[c]);
+        float mx = row_max64(t);
+        if (!bias_tile) mx *= scale_log2;
 
         bool waited_pv = false;
         if (j == 0) {
@@ -389,13 +435,22 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             }
           }
         }
-        float rs = 0.f;
+        const float neg_m = -m;
+        float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (bias_tile) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          t[c] = fast_exp2(t[c] - m);
-          rs += t[c];
+          for (int c = 0; c < BN; ++c) {
+            t[c] = fast_exp2(t[c] + neg_m);
+            part[c & 7] += t[c];
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN; ++c) {
+            t[c] = fast_exp2(fmaf(t[c], scale_log2, neg_m));
+            part[c & 7] += t[c];
+          }
         }
-        l += rs;
+        l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
         // P region is free once the previous tile's PV MMA has completed.
         if (j > 0 && !waited_pv) {
           if (!mbar_wait(&bars->pv_done, pv_iter & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
@@ -406,16 +461,15 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         if (j > 0) ++pv_iter;
         tc_fence_after();
         {
-          uint32_t w[16];
+          uint32_t w0[16], w1[16];
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float lo = t[half * 32 + 2 * e], hi = t[half * 32 + 2 * e + 1];
-              w[e] = (p.dtype == 2) ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-            }
-            tmem_st16(lane_base + kColP + half * 16, w);
+          for (int e = 0; e < 16; ++e) {
+            w0[e] = (p.dtype == 2) ? pack_bf16x2(t[2 * e], t[2 * e + 1]) : pack_f16x2(t[2 * e], t[2 * e + 1]);
+            w1[e] = (p.dtype == 2) ? pack_bf16x2(t[32 + 2 * e], t[33 + 2 * e])
+                                   : pack_f16x2(t[32 + 2 * e], t[33 + 2 * e]);
           }
+          tmem_st16(lane_base + kColP, w0);
+          tmem_st16(lane_base + kColP + 16, w1);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -433,17 +487,22 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       const float inv = 1.f / l;
       uint32_t packed[HD / 2];
       {
-        uint32_t r[16];
+        uint32_t r0[16], r1[16], r2[16], r3[16];
+        tmem_ld16(lane_base + kColO, r0);
+        tmem_ld16(lane_base + kColO + 16, r1);
+        tmem_ld16(lane_base + kColO + 32, r2);
+        tmem_ld16(lane_base + kColO + 48, r3);
+        tmem_wait_ld();
+        reg_fence16(r0);
+        reg_fence16(r1);
+        reg_fence16(r2);
+        reg_fence16(r3);
 #pragma unroll
-        for (int c = 0; c < HD / 16; ++c) {
-          tmem_ld16(lane_base + kColO + c * 16, r);
-          tmem_wait_ld();
-          reg_fence16(r);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float lo = __uint_as_float(r[2 * e]) * inv, hi = __uint_as_float(r[2 * e + 1]) * inv;
-            packed[c * 8 + e] = (p.dtype == 2) ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-          }
+        for (int e = 0; e < 8; ++e) {
+          packed[e] = pack_out(r0[2 * e], r0[2 * e + 1], inv, p.dtype);
+          packed[8 + e] = pack_out(r1[2 * e], r1[2 * e + 1], inv, p.dtype);
+          packed[16 + e] = pack_out(r2[2 * e], r2[2 * e + 1], inv, p.dtype);
+          packed[24 + e] = pack_out(r3[2 * e], r3[2 * e + 1], inv, p.dtype);
         }
       }
       tc_fence_before();
@@ -558,6 +617,7 @@ int32_t sla_tc_supported(const SlaParams& p) {
   if (p.status == nullptr) return 0;
   if (p.seq < 2 || p.seq > (int64_t(1) << 30) || p.batch > (int64_t(1) << 30) || p.heads > (int64_t(1) << 30))
     return 0;
+  if (!(p.scale > 0.f) || !(p.scale < 3.0e38f)) return 0;
   if (!tma_stride_ok(p.q, p.q_stride) || !tma_stride_ok(p.k, p.k_stride) || !tma_stride_ok(p.v, p.v_stride))
     return 0;
   if (reinterpret_cast<uintptr_t>(p.out) % 16 || p.out_stride[3] != 1) return 0;
@@ -580,9 +640,16 @@ int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
   a.n_items = p.batch * p.heads * a.n_qt;
   a.n_slots = p.bias_mode == 2 ? static_cast<int32_t>(p.poses) : 0;
   a.table_bytes = table_bytes_for(a.n_slots);
+  a.pose_vec4 = 0;
+  if (a.n_slots > 0 && p.pose_dtype == 0 && p.pose_stride[3] == 1 && a.n_slots % 4 == 0 &&
+      reinterpret_cast<uintptr_t>(p.pose) % 16 == 0 && p.pose_stride[0] % 4 == 0 && p.pose_stride[1] % 4 == 0 &&
+      p.pose_stride[2] % 4 == 0)
+    a.pose_vec4 = 1;
   const size_t smem = smem_bytes_for(a.table_bytes);
   if (cudaFuncSetAttribute(sla_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-      cudaSuccess)
+          cudaSuccess ||
+      cudaFuncSetAttribute(sla_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return 6;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sla_tc_kernel, kThreads, smem) != cudaSuccess ||
