@@ -90,13 +90,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Row maximum of 64 values as a shallow tree of three-input maxima.
-__device__ __forceinline__ float row_max64(const float (&t)[64]) {
+// Row maximum of 64 values (32 pairs) as a shallow tree of three-input maxima.
+__device__ __forceinline__ float row_max64(const float2 (&t)[32]) {
   float m8[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const float* v = t + 8 * k;
-    m8[k] = fmaxf(fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]), v[6]), v[7]);
+    const float2* v = t + 4 * k;
+    m8[k] = fmaxf(fmax3(fmax3(v[0].x, v[0].y, v[1].x), fmax3(v[1].y, v[2].x, v[2].y), v[3].x), v[3].y);
   }
   return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
 }
@@ -170,7 +170,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       uint32_t kv_iter = 0, item_iter = 0;
-      uint32_t stage_loads[kStages] = {0, 0};
+      uint32_t loads0 = 0, loads1 = 0;  // loads issued into stage 0 / 1
       bool ok = true;
       for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++item_iter) {
         const int64_t qt = item % a.n_qt;
@@ -205,16 +205,15 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           if (bias_tile)
             bulk_load(slot_s + st * kSlotBytes, p.slots_packed + (qt * n_kt + j) * kSlotBytes, kSlotBytes,
                       &bars->kv_full[st]);
-          stage_loads[st] = n + 1;
+          if (st == 0) loads0 = n + 1; else loads1 = n + 1;
         }
       }
       // Drain: never leave a copy in flight into shared memory of an exiting CTA.
-      if (item_iter > 0 || stage_loads[0] > 0) {
+      if (item_iter > 0 || loads0 > 0) {
         volatile int32_t no_abort = 0;
         if (item_iter > 0) mbar_wait(&bars->q_full, (item_iter - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
-        for (int s = 0; s < kStages; ++s)
-          if (stage_loads[s] > 0)
-            mbar_wait(&bars->kv_full[s], (stage_loads[s] - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
+        if (loads0 > 0) mbar_wait(&bars->kv_full[0], (loads0 - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
+        if (loads1 > 0) mbar_wait(&bars->kv_full[1], (loads1 - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
       }
     }
   } else if (warp == 5) {
@@ -346,7 +345,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           break;
         }
         tc_fence_after();
-        float t[BN];
+        float2 t[BN / 2];  // t[c] holds keys 2c and 2c+1
         {
           uint32_t r0[16], r1[16], r2[16], r3[16];
           const uint32_t sa = lane_base + (sb ? kColS1 : kColS0);
@@ -360,11 +359,11 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           reg_fence16(r2);
           reg_fence16(r3);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            t[e] = __uint_as_float(r0[e]);
-            t[16 + e] = __uint_as_float(r1[e]);
-            t[32 + e] = __uint_as_float(r2[e]);
-            t[48 + e] = __uint_as_float(r3[e]);
+          for (int e = 0; e < 8; ++e) {
+            t[e] = make_float2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]));
+            t[8 + e] = make_float2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]));
+            t[16 + e] = make_float2(__uint_as_float(r2[2 * e]), __uint_as_float(r2[2 * e + 1]));
+            t[24 + e] = make_float2(__uint_as_float(r3[2 * e]), __uint_as_float(r3[2 * e + 1]));
           }
         }
         tc_fence_before();
@@ -383,14 +382,17 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           }
           const uint8_t* srow = slot_s + st * kSlotBytes + row * 16;
           const float* trow = table_s + row;
+          const float2 c2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
           for (int c = 0; c < BN / 16; ++c) {
             const uint4 w = *reinterpret_cast<const uint4*>(srow + c * 2048);
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const uint32_t slot = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
-              t[c * 16 + e] = fmaf(t[c * 16 + e], scale_log2, trow[slot * BM]);
+            for (int e = 0; e < 16; e += 2) {
+              const uint32_t s0 = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
+              const uint32_t s1 = __byte_perm(ww[e >> 2], 0u, 0x4440u | ((e + 1) & 3));
+              const float2 bias = make_float2(trow[s0 * BM], trow[s1 * BM]);
+              t[c * 8 + e / 2] = fma2(t[c * 8 + e / 2], c2, bias);
             }
           }
         }
@@ -400,8 +402,10 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         if (j == n_kt - 1) {
           const int64_t key0 = j * BN;
 #pragma unroll
-          for (int c = 0; c < BN; ++c)
-            if (key0 + c >= N) t[c] = -INFINITY;
+          for (int c = 0; c < BN / 2; ++c) {
+            if (key0 + 2 * c >= N) t[c].x = -INFINITY;
+            if (key0 + 2 * c + 1 >= N) t[c].y = -INFINITY;
+          }
         }
         float mx = row_max64(t);
         if (!bias_tile) mx *= scale_log2;
@@ -435,22 +439,21 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             }
           }
         }
-        const float neg_m = -m;
-        float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (bias_tile) {
+        // exponents (log2 domain, relative to the running max), packed pairs
+        const float2 nm2 = make_float2(-m, -m);
+        const float2 c2 = bias_tile ? make_float2(1.f, 1.f) : make_float2(scale_log2, scale_log2);
+        float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            t[c] = fast_exp2(t[c] + neg_m);
-            part[c & 7] += t[c];
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            t[c] = fast_exp2(fmaf(t[c], scale_log2, neg_m));
-            part[c & 7] += t[c];
-          }
+        for (int c = 0; c < BN / 2; ++c) {
+          const float2 x = fma2(t[c], c2, nm2);
+          t[c] = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          part[c & 3] = add2(part[c & 3], t[c]);
         }
-        l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+        {
+          const float2 s01 = add2(add2(part[0], part[1]), add2(part[2], part[3]));
+          l += s01.x + s01.y;
+        }
         // P region is free once the previous tile's PV MMA has completed.
         if (j > 0 && !waited_pv) {
           if (!mbar_wait(&bars->pv_done, pv_iter & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
@@ -464,9 +467,8 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           uint32_t w0[16], w1[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            w0[e] = (p.dtype == 2) ? pack_bf16x2(t[2 * e], t[2 * e + 1]) : pack_f16x2(t[2 * e], t[2 * e + 1]);
-            w1[e] = (p.dtype == 2) ? pack_bf16x2(t[32 + 2 * e], t[33 + 2 * e])
-                                   : pack_f16x2(t[32 + 2 * e], t[33 + 2 * e]);
+            w0[e] = (p.dtype == 2) ? pack_bf16x2(t[e].x, t[e].y) : pack_f16x2(t[e].x, t[e].y);
+            w1[e] = (p.dtype == 2) ? pack_bf16x2(t[16 + e].x, t[16 + e].y) : pack_f16x2(t[16 + e].x, t[16 + e].y);
           }
           tmem_st16(lane_base + kColP, w0);
           tmem_st16(lane_base + kColP + 16, w1);
@@ -651,11 +653,20 @@ int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
       cudaFuncSetAttribute(sla_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                            cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return 6;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sla_tc_kernel, kThreads, smem) != cudaSuccess ||
-      per_sm < 1)
+  // Resident CTAs per SM from the register and shared-memory budgets (the
+  // occupancy query does not account for the carveout set above).
+  int dev = 0, smem_per_sm = 0, regs_per_sm = 0;
+  cudaFuncAttributes fa;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaFuncGetAttributes(&fa, sla_tc_kernel) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&regs_per_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess)
     return 6;
-  if (per_sm > 2) per_sm = 2;
+  const int warp_regs = ((fa.numRegs * 32 + 255) / 256) * 256;
+  const int by_regs = regs_per_sm / (warp_regs * (kThreads / 32));
+  const int by_smem = smem_per_sm / static_cast<int>(smem + 1024);
+  int per_sm = by_regs < by_smem ? by_regs : by_smem;
+  if (per_sm > 2) per_sm = 2;  // two 256-column TMEM allocations per SM
+  if (per_sm < 1) return 6;
   int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
   if (grid > a.n_items) grid = a.n_items;
   sla_tc_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(mq, mk, mv, a);
