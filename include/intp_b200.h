@@ -122,6 +122,36 @@ INTP_API intp_status nl1_forward(const float* x, const float* w, float* out,
  * (synchronous on `stream`) and clears it.  *code = 0 when no wait failed.  */
 INTP_API intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream);
 
+/* Longest sequence (tokens, CLS included) sla_forward_noalloc accepts. */
+#define SLA_NOALLOC_MAX_SEQ 1025
+
+/* Look-attention forward that allocates nothing, for callers that cannot
+ * allocate device memory: plugins whose enqueue step must not allocate
+ * because the host framework plans all memory ahead of time, serving loops
+ * that forbid allocation after start-up, and callers with a fixed memory
+ * budget.  No counterpart in the reference (its Triton launch allocates its
+ * outputs itself); this entry point has no reference citation for that reason.
+ *
+ * Same arguments as sla_forward in SLOTS mode on the tensor-core path (bf16 or
+ * f16, head_dim 64), except that `slots` is the plain (Np x Np) uint8 slot
+ * table in device memory (SLA_SLOT_NONE = no bias; other values >= n_slots
+ * are also taken as no bias); args->slots_packed and args->slot_tile_flags
+ * are ignored.  The table is packed on the GPU into a library-owned
+ * file-scope __device__ scratch array of about 1.2 MB, which every GPU that
+ * loads the library holds until the process exits.  args->status may point
+ * at a caller-owned int32 that receives bounded-wait failures; when it is
+ * NULL they are recorded in the scratch instead.
+ *
+ * Limits and behaviour:
+ *   - seq > SLA_NOALLOC_MAX_SEQ, or a request the tensor-core path cannot
+ *     take, returns INTP_ERR_UNSUPPORTED without launching anything.
+ *   - The first call on each device resolves the scratch address with that
+ *     device current; make that first call before any stream capture.
+ *   - Every call shares the scratch and leaves its contents behind; calls
+ *     whose work overlaps on the GPU (several streams or threads) race.
+ *   - Calls no cudaMalloc / cudaFree and no allocating library routine.      */
+INTP_API intp_status sla_forward_noalloc(const sla_forward_args* args, const uint8_t* slots, void* stream);
+
 /* Library / device facts: compute capability of the current device and the
  * library's ABI version.                                                    */
 INTP_API intp_status intp_device_info(int32_t* sm_major, int32_t* sm_minor, int32_t* sm_count);

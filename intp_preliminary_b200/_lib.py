@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "sla_pack_slot_table",
     "nl1_forward",
     "sla_read_status",
+    "sla_forward_noalloc",
     "intp_device_info",
     "intp_abi_version",
     "intp_status_string",
@@ -100,6 +101,8 @@ def load() -> ctypes.CDLL:
         lib.sla_pack_slot_table.restype = _i32
         lib.nl1_forward.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
         lib.nl1_forward.restype = _i32
+        lib.sla_forward_noalloc.argtypes = [ctypes.POINTER(SlaForwardArgs), _vp, _vp]
+        lib.sla_forward_noalloc.restype = _i32
         lib.sla_read_status.argtypes = [_vp, ctypes.POINTER(_i32), _vp]
         lib.sla_read_status.restype = _i32
         lib.intp_device_info.argtypes = [ctypes.POINTER(_i32)] * 3
