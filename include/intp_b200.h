@@ -104,7 +104,9 @@ INTP_API intp_status sla_forward(const sla_forward_args* args, void* stream);
 INTP_API intp_status sla_slot_table_bytes(int64_t seq, int64_t* packed_bytes, int64_t* flag_bytes);
 
 /* Host-side packing of a (Np x Np) uint8 slot table (SLA_SLOT_NONE = no bias,
- * other values < n_slots) into the tile layout the kernels read.  Pure CPU:
+ * other values < n_slots <= 253) into the tile layout the kernels read
+ * (tiles of 128 query x 64 key tokens; entry n_slots = no bias, n_slots + 1 =
+ * key past the sequence end, which the kernels treat as masked).  Pure CPU:
  * both outputs are host buffers of the sizes sla_slot_table_bytes returns.
  * Stands in for the one-hot `fields` tensor of the reference API
  * (layers/triton_structured_look_attention.py:116-130 loads it per pair).   */

@@ -82,11 +82,13 @@ intp_status sla_slot_table_bytes(int64_t seq, int64_t* packed_bytes, int64_t* fl
 }
 
 // Packs a patch-indexed (Np x Np) slot table into token-indexed tiles: token i
-// = patch i-1, token 0 (CLS) and padding carry n_slots ("no bias").
+// = patch i-1; token 0 (CLS), unslotted pairs and padding query rows carry
+// n_slots ("no bias"); key columns past the sequence end carry n_slots + 1
+// ("padding key", looked up as -inf so the kernel needs no per-key mask).
 intp_status sla_pack_slot_table(const uint8_t* slots, int64_t patch_count, int32_t n_slots, uint8_t* packed,
                                 uint8_t* tile_flags) {
   if (!slots || !packed || !tile_flags || patch_count < 0) return INTP_ERR_ARGUMENT;
-  if (n_slots < 1 || n_slots > 254) return INTP_ERR_ARGUMENT;
+  if (n_slots < 1 || n_slots > 253) return INTP_ERR_ARGUMENT;
   const int64_t seq = patch_count + 1;
   int64_t pb = 0, fb = 0;
   sla_slot_table_bytes(seq, &pb, &fb);
@@ -104,7 +106,18 @@ intp_status sla_pack_slot_table(const uint8_t* slots, int64_t patch_count, int32
       const int64_t kt = j / intp::kSlotTileK, c = j % intp::kSlotTileK;
       const int64_t off = (qt * nkt + kt) * intp::kSlotTileBytes + (c / 16) * 2048 + r * 16 + (c % 16);
       packed[off] = s;
-      tile_flags[qt * nkt + kt] = 1;
+      tile_flags[qt * nkt + kt] |= static_cast<uint8_t>(1u << (r / 32));  // bit w: rows 32w..32w+31
+    }
+  }
+  if (seq % intp::kSlotTileK != 0) {
+    const int64_t nqt = (seq + intp::kSlotTileQ - 1) / intp::kSlotTileQ;
+    const int64_t kt = nkt - 1;
+    for (int64_t qt = 0; qt < nqt; ++qt) {
+      for (int64_t c = seq % intp::kSlotTileK; c < intp::kSlotTileK; ++c)
+        for (int64_t r = 0; r < intp::kSlotTileQ; ++r)
+          packed[(qt * nkt + kt) * intp::kSlotTileBytes + (c / 16) * 2048 + r * 16 + (c % 16)] =
+              static_cast<uint8_t>(n_slots + 1);
+      tile_flags[qt * nkt + kt] |= 0xF;  // every row sees the masked keys
     }
   }
   return INTP_OK;
@@ -122,7 +135,7 @@ intp_status sla_forward(const sla_forward_args* a, void* stream) {
     if (!a->pose || !a->fields || a->poses < 1) return INTP_ERR_ARGUMENT;
     if (!valid_dtype(a->pose_dtype) || !valid_dtype(a->fields_dtype)) return INTP_ERR_DTYPE;
   } else if (a->bias_mode == SLA_BIAS_SLOTS) {
-    if (!a->pose || !a->slots_packed || !a->slot_tile_flags || a->poses < 1 || a->poses > 254)
+    if (!a->pose || !a->slots_packed || !a->slot_tile_flags || a->poses < 1 || a->poses > 253)
       return INTP_ERR_ARGUMENT;
     if (!valid_dtype(a->pose_dtype)) return INTP_ERR_DTYPE;
   } else if (a->bias_mode != SLA_BIAS_NONE) {

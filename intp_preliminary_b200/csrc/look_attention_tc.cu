@@ -8,14 +8,21 @@
 // CTA organisation (192 threads, two CTAs per SM):
 //   warps 0-3  softmax warpgroup: thread t owns query row t of the 128-row tile.
 //              Reads S from TMEM, adds the Look bias from shared memory, runs the
-//              online softmax in the log2 domain, writes P (16-bit) back to TMEM,
-//              rescales O in TMEM when the running max grows by more than 2^8,
-//              and finally normalises O and stores it (plus the LSE).
-//   warp 4     TMA producer: Q tile (128 x 64) per work item, then K/V tiles of
-//              64 keys plus the 8 KB packed slot tile, double buffered.
+//              online softmax in the log2 domain and writes P (16-bit) back into
+//              the same TMEM columns S came from.  O is rescaled in TMEM only
+//              when the running max grows by more than 2^8.  At the end of an
+//              item it normalises O and stores it (plus the LSE).
+//   warp 4     TMA producer: Q tile (128 x 64) per work item, then K tiles of
+//              64 keys with their 8 KB packed slot tiles (3-stage ring, freed
+//              once S(j) is computed and its slots are read) and V tiles
+//              (2-stage ring, freed once PV(j) completes).
 //   warp 5     MMA issuer: S = Q K^T (tcgen05.mma kind::f16, both operands in
-//              shared memory, accumulator in TMEM) and O += P V (P from TMEM).
-// TMEM columns: [0,64) S buffer 0, [64,128) S buffer 1, [128,192) O, [192,224) P.
+//              shared memory, accumulator in TMEM) and O += P [V | 1] with P read
+//              from TMEM.  The extra B block is a constant column of ones, so O
+//              column 64 accumulates the softmax row sum on the tensor core.
+// TMEM columns: [0,64) S / P buffer 0, [64,128) S / P buffer 1, [128,208) O
+// (64 output columns + the row-sum column + 15 unused).  An S buffer is reused
+// for tile j+2 only after PV(j), which reads P(j) from it, has completed.
 //
 // The CTA is persistent over work items (batch, head, 128-row query tile).
 // Every mbarrier wait is bounded (sm100_ptx.cuh); on expiry the CTA unwinds,
@@ -34,23 +41,28 @@ namespace {
 constexpr int BM = 128;            // query rows per tile
 constexpr int BN = 64;             // keys per tile
 constexpr int HD = 64;             // head_dim
+constexpr int ON = HD + 16;        // PV MMA N: 64 outputs + the ones block (row sum in column 64)
 constexpr int kThreads = 192;
-constexpr int kStages = 2;
+constexpr int kKStages = 3;   // K tile + slot tile ring (released after S(j) and the slot reads)
+constexpr int kVStages = 2;   // V tile ring (released after PV(j))
 constexpr uint32_t kQBytes = BM * HD * 2;      // 16 KB
-constexpr uint32_t kKVBytes = BN * HD * 2;     // 8 KB each of K and V
+constexpr uint32_t kKVBytes = BN * HD * 2;     // 8 KB each of K and V (and the ones tile)
 constexpr uint32_t kSlotBytes = kSlotTileBytes;  // 8 KB
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128, kColP = 192;
+constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 2^8
-constexpr int kMaxSlots = 94;
+constexpr int kMaxSlots = 93;
 
 struct alignas(8) Barriers {
   uint64_t q_full, q_empty;
-  uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full, pv_done;
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full[kVStages], v_empty[kVStages];
+  // s_full[b]: S of a tile is in buffer b.  p_full[b]: its P is stored there.
+  // pv_done[b]: the PV that read that P finished (buffer b is free again).
+  // One barrier per buffer keeps every waiter at most one phase behind.
+  uint64_t s_full[2], p_full[2], pv_done[2];
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
@@ -60,9 +72,10 @@ struct SmemLayout {
   // offsets relative to a 1024-byte aligned base
   static constexpr uint32_t q = 0;
   static constexpr uint32_t k = q + kQBytes;
-  static constexpr uint32_t v = k + kStages * kKVBytes;
-  static constexpr uint32_t slots = v + kStages * kKVBytes;
-  static constexpr uint32_t table = slots + kStages * kSlotBytes;
+  static constexpr uint32_t v = k + kKStages * kKVBytes;
+  static constexpr uint32_t ones = v + kVStages * kKVBytes;  // constant [keys][64] tile, column 0 = 1
+  static constexpr uint32_t slots = ones + kKVBytes;
+  static constexpr uint32_t table = slots + kKStages * kSlotBytes;
 };
 
 __device__ __forceinline__ float load_any(const void* p, int64_t idx, int32_t dtype) {
@@ -119,11 +132,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment (128B-swizzle tiles) by an offset from the __shared__
+  // array itself, so every derived pointer stays in the shared address space
+  // (32-bit LDS/STS instead of generic 64-bit loads).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Barriers* bars = reinterpret_cast<Barriers*>(smem + SmemLayout::table + a.table_bytes);
   uint8_t* q_s = smem + SmemLayout::q;
   uint8_t* k_s = smem + SmemLayout::k;
   uint8_t* v_s = smem + SmemLayout::v;
+  uint8_t* ones_s = smem + SmemLayout::ones;
   uint8_t* slot_s = smem + SmemLayout::slots;
   float* table_s = reinterpret_cast<float*>(smem + SmemLayout::table);
 
@@ -135,19 +152,34 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->q_empty, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1 + 4);  // MMA commit + 4 softmax warps
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1 + 4);  // S-MMA commit + 4 softmax warps (slot reads)
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);  // PV-MMA commit
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], 4);
+      mbar_init(&bars->p_full[s], 4);
+      mbar_init(&bars->pv_done[s], 1);
     }
-    mbar_init(&bars->p_full, 4);
-    mbar_init(&bars->pv_done, 1);
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     mbar_fence_init();
+  }
+  // The ones tile: a 64-key x 64-column bf16/f16 block in the same 128B-swizzled
+  // layout TMA gives V, with logical column 0 equal to 1 and every other column 0.
+  if (warp < 4) {
+    const uint16_t one = p.dtype == 2 ? uint16_t(0x3F80) : uint16_t(0x3C00);
+    for (int w = threadIdx.x; w < static_cast<int>(kKVBytes / 16); w += 128) {
+      const int r = w >> 3, chunk = w & 7;  // 16-byte chunk `chunk` of key row r
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (chunk == (r & 7)) v.x = one;      // logical chunk 0 lands at physical chunk r % 8
+      reinterpret_cast<uint4*>(ones_s)[w] = v;
+    }
+    fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor core
   }
   if (warp == 5) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -165,13 +197,25 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
+    // K tiles (with their slot tiles) run up to kKStages ahead; V tiles lag one
+    // key tile behind K so a V stage still in use never blocks the next K load.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      uint32_t kv_iter = 0, item_iter = 0;
-      uint32_t loads0 = 0, loads1 = 0;  // loads issued into stage 0 / 1
+      uint32_t k_iter = 0, v_iter = 0, item_iter = 0;
       bool ok = true;
+      auto load_v = [&](int64_t jv, int32_t h, int32_t b) -> bool {
+        const uint32_t vs = v_iter % kVStages, n = v_iter / kVStages;
+        if (n > 0 && !mbar_wait(&bars->v_empty[vs], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer))
+          return false;
+        mbar_arrive_expect_tx(&bars->v_full[vs], kKVBytes);
+        const int32_t r = static_cast<int32_t>(jv * BN);
+        tma_load_4d(v_s + vs * kKVBytes, &tm_v, &bars->v_full[vs], 0, map_coord(a.ov, 1, r, h, b),
+                    map_coord(a.ov, 2, r, h, b), map_coord(a.ov, 3, r, h, b));
+        ++v_iter;
+        return true;
+      };
       for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++item_iter) {
         const int64_t qt = item % a.n_qt;
         const int64_t bh = item / a.n_qt;
@@ -187,33 +231,39 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           tma_load_4d(q_s, &tm_q, &bars->q_full, 0, map_coord(a.oq, 1, r, h, b), map_coord(a.oq, 2, r, h, b),
                       map_coord(a.oq, 3, r, h, b));
         }
-        for (int64_t j = 0; j < n_kt; ++j, ++kv_iter) {
-          const uint32_t st = kv_iter % kStages, n = kv_iter / kStages;
-          if (n > 0 && !mbar_wait(&bars->kv_empty[st], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer)) {
+        for (int64_t j = 0; j < n_kt; ++j) {
+          const uint32_t ks = k_iter % kKStages, n = k_iter / kKStages;
+          if (n > 0 && !mbar_wait(&bars->k_empty[ks], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
           const bool bias_tile = use_bias && p.slot_tile_flags[qt * n_kt + j];
-          mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kKVBytes + (bias_tile ? kSlotBytes : 0));
-          {
-            const int32_t r = static_cast<int32_t>(j * BN);
-            tma_load_4d(k_s + st * kKVBytes, &tm_k, &bars->kv_full[st], 0, map_coord(a.ok, 1, r, h, b),
-                        map_coord(a.ok, 2, r, h, b), map_coord(a.ok, 3, r, h, b));
-            tma_load_4d(v_s + st * kKVBytes, &tm_v, &bars->kv_full[st], 0, map_coord(a.ov, 1, r, h, b),
-                        map_coord(a.ov, 2, r, h, b), map_coord(a.ov, 3, r, h, b));
-          }
+          mbar_arrive_expect_tx(&bars->k_full[ks], kKVBytes + (bias_tile ? kSlotBytes : 0));
+          const int32_t r = static_cast<int32_t>(j * BN);
+          tma_load_4d(k_s + ks * kKVBytes, &tm_k, &bars->k_full[ks], 0, map_coord(a.ok, 1, r, h, b),
+                      map_coord(a.ok, 2, r, h, b), map_coord(a.ok, 3, r, h, b));
           if (bias_tile)
-            bulk_load(slot_s + st * kSlotBytes, p.slots_packed + (qt * n_kt + j) * kSlotBytes, kSlotBytes,
-                      &bars->kv_full[st]);
-          if (st == 0) loads0 = n + 1; else loads1 = n + 1;
+            bulk_load(slot_s + ks * kSlotBytes, p.slots_packed + (qt * n_kt + j) * kSlotBytes, kSlotBytes,
+                      &bars->k_full[ks]);
+          ++k_iter;
+          if (j > 0 && !load_v(j - 1, h, b)) {
+            ok = false;
+            break;
+          }
         }
+        if (ok && !load_v(n_kt - 1, h, b)) ok = false;
       }
       // Drain: never leave a copy in flight into shared memory of an exiting CTA.
-      if (item_iter > 0 || loads0 > 0) {
-        volatile int32_t no_abort = 0;
-        if (item_iter > 0) mbar_wait(&bars->q_full, (item_iter - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
-        if (loads0 > 0) mbar_wait(&bars->kv_full[0], (loads0 - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
-        if (loads1 > 0) mbar_wait(&bars->kv_full[1], (loads1 - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
+      // Stage s of a ring with `issued` loads received (issued - s + R - 1) / R of them.
+      volatile int32_t no_abort = 0;
+      if (item_iter > 0) mbar_wait(&bars->q_full, (item_iter - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
+      for (uint32_t st = 0; st < kKStages; ++st) {
+        const uint32_t cnt = k_iter > st ? (k_iter - st + kKStages - 1) / kKStages : 0;
+        if (cnt > 0) mbar_wait(&bars->k_full[st], (cnt - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
+      }
+      for (uint32_t st = 0; st < kVStages; ++st) {
+        const uint32_t cnt = v_iter > st ? (v_iter - st + kVStages - 1) / kVStages : 0;
+        if (cnt > 0) mbar_wait(&bars->v_full[st], (cnt - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
       }
     }
   } else if (warp == 5) {
@@ -221,24 +271,53 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     if (lane == 0) {
       const bool bf16 = p.dtype == 2;
       const uint32_t idesc_qk = idesc_f16(bf16, false, BM, BN);
-      const uint32_t idesc_pv = idesc_f16(bf16, true, BM, HD);
-      const uint32_t q_addr = smem_u32(q_s), k_addr = smem_u32(k_s), v_addr = smem_u32(v_s);
-      uint32_t kv_iter = 0, s_iter = 0, pv_iter = 0, item_iter = 0;
+      const uint32_t idesc_pv = idesc_f16(bf16, true, BM, ON);
+      // Descriptors are built once; a K step / stage advances only the 14-bit
+      // start-address field (16-byte units) in the low word, which cannot carry.
+      // V is MN-major with two 64-wide column blocks: the V tile and, LBO bytes
+      // further, the constant ones tile.
+      const uint32_t v_addr = smem_u32(v_s), ones_addr = smem_u32(ones_s);
+      const uint64_t q_desc = smem_desc_sw128(smem_u32(q_s), 16, 1024);
+      const uint64_t k_desc = smem_desc_sw128(smem_u32(k_s), 16, 1024);
+      const uint64_t v_desc0 = smem_desc_sw128(v_addr, ones_addr - v_addr, 1024);
+      const uint64_t v_desc1 = smem_desc_sw128(v_addr + kKVBytes, ones_addr - (v_addr + kKVBytes), 1024);
+      uint32_t k_iter = 0, v_iter = 0, s_iter = 0, pv_iter = 0, item_iter = 0;
       bool ok = true, issued = false;
+      // O += P [V | 1] for the tile whose P the softmax just published (global tile pv_iter).
+      auto issue_pv = [&](bool first_tile) -> bool {
+        const uint32_t pb = pv_iter & 1;
+        if (!mbar_wait(&bars->p_full[pb], (pv_iter >> 1) & 1, abort_flag, p.status, kDevTimeoutMma)) return false;
+        const uint32_t vs = v_iter % kVStages;
+        if (!mbar_wait(&bars->v_full[vs], (v_iter / kVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
+          return false;
+        tc_fence_after();
+        const uint64_t vd = vs == 0 ? v_desc0 : v_desc1;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ts(tmem + kColO, tmem + (pb ? kColS1 : kColS0) + kk * 8, vd + ((kk * 2048) >> 4), idesc_pv,
+                 (!first_tile || kk > 0) ? 1u : 0u);
+        mma_commit(&bars->pv_done[pb]);
+        mma_commit(&bars->v_empty[vs]);
+        ++pv_iter;
+        ++v_iter;
+        return true;
+      };
       for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++item_iter) {
         if (!mbar_wait(&bars->q_full, item_iter & 1, abort_flag, p.status, kDevTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        for (int64_t j = 0; j < n_kt && ok; ++j, ++kv_iter) {
-          const uint32_t st = kv_iter % kStages;
-          if (!mbar_wait(&bars->kv_full[st], (kv_iter / kStages) & 1, abort_flag, p.status, kDevTimeoutMma)) {
+        for (int64_t j = 0; j < n_kt && ok; ++j) {
+          const uint32_t ks = k_iter % kKStages;
+          if (!mbar_wait(&bars->k_full[ks], (k_iter / kKStages) & 1, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
-          const uint32_t sb = s_iter & 1, su = s_iter >> 1;
-          if (su > 0 && !mbar_wait(&bars->s_free[sb], (su - 1) & 1, abort_flag, p.status, kDevTimeoutMma)) {
+          // S buffer sb last held P of tile s_iter - 2: its PV must be done.
+          const uint32_t sb = s_iter & 1;
+          if (s_iter >= 2 &&
+              !mbar_wait(&bars->pv_done[sb], ((s_iter - 2) >> 1) & 1, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -246,46 +325,26 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           const uint32_t s_col = tmem + (sb ? kColS1 : kColS0);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(k_addr + st * kKVBytes + kk * 32, 16, 1024);
+            const uint64_t ad = q_desc + ((kk * 32) >> 4);
+            const uint64_t bd = k_desc + ((ks * kKVBytes + kk * 32) >> 4);
             mma_ss(s_col, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
           }
           mma_commit(&bars->s_full[sb]);
+          mma_commit(&bars->k_empty[ks]);
           issued = true;
           ++s_iter;
-          if (j > 0) {
-            if (!mbar_wait(&bars->p_full, pv_iter & 1, abort_flag, p.status, kDevTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t pst = (kv_iter - 1) % kStages;
-#pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t bd = smem_desc_sw128(v_addr + pst * kKVBytes + kk * 2048, 8192, 1024);
-              mma_ts(tmem + kColO, tmem + kColP + kk * 8, bd, idesc_pv, (j - 1 > 0 || kk > 0) ? 1u : 0u);
-            }
-            mma_commit(&bars->pv_done);
-            mma_commit(&bars->kv_empty[pst]);
-            ++pv_iter;
+          ++k_iter;
+          if (j > 0 && !issue_pv(j == 1)) {
+            ok = false;
+            break;
           }
         }
         if (!ok) break;
         mma_commit(&bars->q_empty);
-        if (!mbar_wait(&bars->p_full, pv_iter & 1, abort_flag, p.status, kDevTimeoutMma)) {
+        if (!issue_pv(n_kt == 1)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t lst = (kv_iter - 1) % kStages;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = smem_desc_sw128(v_addr + lst * kKVBytes + kk * 2048, 8192, 1024);
-          mma_ts(tmem + kColO, tmem + kColP + kk * 8, bd, idesc_pv, (n_kt - 1 > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&bars->pv_done);
-        mma_commit(&bars->kv_empty[lst]);
-        ++pv_iter;
       }
       // Drain: all issued MMAs must finish before TMEM is released.
       if (issued) {
@@ -300,7 +359,12 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const float scale_log2 = p.scale * kLog2e;  // > 0 (checked on the host)
     const int32_t ns = a.n_slots;
-    uint32_t s_iter = 0, kv_iter = 0, pv_iter = 0;
+    uint32_t k_iter = 0;
+    uint32_t g = 0;  // global index of the key tile being processed (S/P buffer g & 1)
+    // Waits until the PV MMA of global tile t (buffer t & 1) has completed.
+    auto wait_pv = [&](uint32_t t) -> bool {
+      return mbar_wait(&bars->pv_done[t & 1], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax);
+    };
     bool ok = true;
     for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x) {
       const int64_t qt = item % a.n_qt;
@@ -326,33 +390,34 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             table_s[s * BM + row] =
                 valid ? load_any(p.pose, base + s * p.pose_stride[3], p.pose_dtype) * kLog2e : 0.f;
         }
-        table_s[ns * BM + row] = 0.f;
+        table_s[ns * BM + row] = 0.f;               // "no bias"
+        table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
       }
-      float m = -INFINITY, l = 0.f;
-      uint64_t tile_mask = 0;  // bit k: key tile (j & ~63) + k carries Look bias
-      for (int64_t j = 0; j < n_kt; ++j, ++kv_iter) {
+      float m = -INFINITY;
+      uint64_t tile_mask = 0;  // bit k: key tile (j & ~63) + k carries Look bias for this warp
+      for (int64_t j = 0; j < n_kt; ++j, ++k_iter) {
         if (use_bias && (j & 63) == 0) {
           // Each warp gathers the flags of the next 64 key tiles with one ballot pair.
           const int64_t t0 = j + lane, t1 = j + 32 + lane;
-          const bool f0 = t0 < n_kt && p.slot_tile_flags[qt * n_kt + t0] != 0;
-          const bool f1 = t1 < n_kt && p.slot_tile_flags[qt * n_kt + t1] != 0;
+          const bool f0 = t0 < n_kt && ((p.slot_tile_flags[qt * n_kt + t0] >> warp) & 1);
+          const bool f1 = t1 < n_kt && ((p.slot_tile_flags[qt * n_kt + t1] >> warp) & 1);
           tile_mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, f0)) |
                       (static_cast<uint64_t>(__ballot_sync(0xffffffffu, f1)) << 32);
         }
-        const uint32_t sb = s_iter & 1;
-        if (!mbar_wait(&bars->s_full[sb], (s_iter >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+        const uint32_t sb = g & 1;
+        if (!mbar_wait(&bars->s_full[sb], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t s_addr = lane_base + (sb ? kColS1 : kColS0);
         float2 t[BN / 2];  // t[c] holds keys 2c and 2c+1
         {
           uint32_t r0[16], r1[16], r2[16], r3[16];
-          const uint32_t sa = lane_base + (sb ? kColS1 : kColS0);
-          tmem_ld16(sa, r0);
-          tmem_ld16(sa + 16, r1);
-          tmem_ld16(sa + 32, r2);
-          tmem_ld16(sa + 48, r3);
+          tmem_ld16(s_addr, r0);
+          tmem_ld16(s_addr + 16, r1);
+          tmem_ld16(s_addr + 32, r2);
+          tmem_ld16(s_addr + 48, r3);
           tmem_wait_ld();
           reg_fence16(r0);
           reg_fence16(r1);
@@ -366,23 +431,18 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             t[24 + e] = make_float2(__uint_as_float(r3[2 * e]), __uint_as_float(r3[2 * e + 1]));
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->s_free[sb]);
-        ++s_iter;
 
         // t holds raw scores on tiles without Look bias, and the log2-domain
         // logits scale*log2(e)*s + bias on tiles with it.
-        const uint32_t st = kv_iter % kStages;
+        const uint32_t st = k_iter % kKStages;
         const bool bias_tile = (tile_mask >> (j & 63)) & 1u;
         if (bias_tile) {
-          if (!mbar_wait(&bars->kv_full[st], (kv_iter / kStages) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+          if (!mbar_wait(&bars->k_full[st], (k_iter / kKStages) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
             ok = false;
             break;
           }
           const uint8_t* srow = slot_s + st * kSlotBytes + row * 16;
           const float* trow = table_s + row;
-          const float2 c2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
           for (int c = 0; c < BN / 16; ++c) {
             const uint4 w = *reinterpret_cast<const uint4*>(srow + c * 2048);
@@ -391,41 +451,45 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             for (int e = 0; e < 16; e += 2) {
               const uint32_t s0 = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
               const uint32_t s1 = __byte_perm(ww[e >> 2], 0u, 0x4440u | ((e + 1) & 3));
-              const float2 bias = make_float2(trow[s0 * BM], trow[s1 * BM]);
-              t[c * 8 + e / 2] = fma2(t[c * 8 + e / 2], c2, bias);
+              float2& tv = t[c * 8 + e / 2];
+              tv.x = fmaf(tv.x, scale_log2, trow[s0 * BM]);
+              tv.y = fmaf(tv.y, scale_log2, trow[s1 * BM]);
             }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->kv_empty[st]);
+        if (lane == 0) mbar_arrive(&bars->k_empty[st]);
 
-        if (j == n_kt - 1) {
-          const int64_t key0 = j * BN;
+        // Keys past the sequence end: the slot path looks them up as -inf (the
+        // packed table marks them); without a Look bias mask them here.
+        if (!use_bias) {
+          const int32_t valid = static_cast<int32_t>(N - j * BN < BN ? N - j * BN : BN);
+          if (valid < BN) {
 #pragma unroll
-          for (int c = 0; c < BN / 2; ++c) {
-            if (key0 + 2 * c >= N) t[c].x = -INFINITY;
-            if (key0 + 2 * c + 1 >= N) t[c].y = -INFINITY;
+            for (int c = 0; c < BN / 2; ++c) {
+              if (2 * c >= valid) t[c].x = -INFINITY;
+              if (2 * c + 1 >= valid) t[c].y = -INFINITY;
+            }
           }
         }
         float mx = row_max64(t);
         if (!bias_tile) mx *= scale_log2;
 
-        bool waited_pv = false;
         if (j == 0) {
           m = mx;
         } else {
           const bool need = mx > m + kRescaleThreshold;
           if (__any_sync(0xffffffffu, need)) {
-            if (!mbar_wait(&bars->pv_done, pv_iter & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+            // O is read-modify-written: every PV issued so far (up to tile g-1) must be done.
+            if (!wait_pv(g - 1)) {
               ok = false;
               break;
             }
-            waited_pv = true;
             tc_fence_after();
             const float f = need ? fast_exp2(m - mx) : 1.f;
             uint32_t r[16];
 #pragma unroll
-            for (int c = 0; c < HD / 16; ++c) {
+            for (int c = 0; c < ON / 16; ++c) {
               tmem_ld16(lane_base + kColO + c * 16, r);
               tmem_wait_ld();
               reg_fence16(r);
@@ -433,72 +497,56 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
               for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
               tmem_st16(lane_base + kColO + c * 16, r);
             }
-            if (need) {
-              l *= f;
-              m = mx;
-            }
+            if (need) m = mx;
           }
         }
-        // exponents (log2 domain, relative to the running max), packed pairs
-        const float2 nm2 = make_float2(-m, -m);
-        const float2 c2 = bias_tile ? make_float2(1.f, 1.f) : make_float2(scale_log2, scale_log2);
-        float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                          make_float2(0.f, 0.f)};
+        // Probabilities (log2 domain, relative to the running max), written as
+        // 16-bit pairs over the S columns they came from.  The row sum is not
+        // kept here: the PV MMA accumulates it into O column 64.
+        const float cs = bias_tile ? 1.f : scale_log2;
+        const float2 c2 = make_float2(cs, cs), nm2 = make_float2(-m, -m);
+        uint32_t w0[16], w1[16];
 #pragma unroll
-        for (int c = 0; c < BN / 2; ++c) {
-          const float2 x = fma2(t[c], c2, nm2);
-          t[c] = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-          part[c & 3] = add2(part[c & 3], t[c]);
+        for (int e = 0; e < 16; ++e) {
+          const float2 x0 = fma2(t[e], c2, nm2);
+          const float2 x1 = fma2(t[16 + e], c2, nm2);
+          const float p0 = fast_exp2(x0.x), p1 = fast_exp2(x0.y);
+          const float p2 = fast_exp2(x1.x), p3 = fast_exp2(x1.y);
+          w0[e] = (p.dtype == 2) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+          w1[e] = (p.dtype == 2) ? pack_bf16x2(p2, p3) : pack_f16x2(p2, p3);
         }
-        {
-          const float2 s01 = add2(add2(part[0], part[1]), add2(part[2], part[3]));
-          l += s01.x + s01.y;
-        }
-        // P region is free once the previous tile's PV MMA has completed.
-        if (j > 0 && !waited_pv) {
-          if (!mbar_wait(&bars->pv_done, pv_iter & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
-            ok = false;
-            break;
-          }
-        }
-        if (j > 0) ++pv_iter;
-        tc_fence_after();
-        {
-          uint32_t w0[16], w1[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            w0[e] = (p.dtype == 2) ? pack_bf16x2(t[e].x, t[e].y) : pack_f16x2(t[e].x, t[e].y);
-            w1[e] = (p.dtype == 2) ? pack_bf16x2(t[16 + e].x, t[16 + e].y) : pack_f16x2(t[16 + e].x, t[16 + e].y);
-          }
-          tmem_st16(lane_base + kColP, w0);
-          tmem_st16(lane_base + kColP + 16, w1);
-        }
+        tmem_st16(s_addr, w0);
+        tmem_st16(s_addr + 16, w1);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_full);
+        if (lane == 0) mbar_arrive(&bars->p_full[g & 1]);
+        ++g;
       }
       if (!ok) break;
-      // Epilogue: wait for the item's last PV, normalise, store.
-      if (!mbar_wait(&bars->pv_done, pv_iter & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+      // Epilogue: wait for the item's last PV, normalise by the row sum (O column 64), store.
+      if (!wait_pv(g - 1)) {
         ok = false;
         break;
       }
-      ++pv_iter;
       tc_fence_after();
-      const float inv = 1.f / l;
       uint32_t packed[HD / 2];
+      float l;
       {
-        uint32_t r0[16], r1[16], r2[16], r3[16];
+        uint32_t r0[16], r1[16], r2[16], r3[16], r4[16];
         tmem_ld16(lane_base + kColO, r0);
         tmem_ld16(lane_base + kColO + 16, r1);
         tmem_ld16(lane_base + kColO + 32, r2);
         tmem_ld16(lane_base + kColO + 48, r3);
+        tmem_ld16(lane_base + kColO + 64, r4);
         tmem_wait_ld();
         reg_fence16(r0);
         reg_fence16(r1);
         reg_fence16(r2);
         reg_fence16(r3);
+        reg_fence16(r4);
+        l = __uint_as_float(r4[0]);
+        const float inv = 1.f / l;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           packed[e] = pack_out(r0[2 * e], r0[2 * e + 1], inv, p.dtype);
@@ -598,7 +646,7 @@ bool tma_stride_ok(const void* base, const int64_t* stride) {
 }
 
 uint32_t table_bytes_for(int32_t n_slots) {
-  return n_slots > 0 ? static_cast<uint32_t>((n_slots + 1) * BM * sizeof(float)) : 0u;
+  return n_slots > 0 ? static_cast<uint32_t>((n_slots + 2) * BM * sizeof(float)) : 0u;
 }
 
 size_t smem_bytes_for(uint32_t table_bytes) {

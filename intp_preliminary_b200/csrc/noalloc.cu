@@ -68,31 +68,39 @@ const DeviceScratch* scratch_for_current_device() {
 }
 
 // Packs a patch-indexed (Np x Np) slot table into the token-indexed tile layout
-// of sla_pack_slot_table (token i = patch i-1; CLS row/column, padding and
-// SLA_SLOT_NONE become n_slots) and writes one "has bias" flag per tile.  One
+// of sla_pack_slot_table (token i = patch i-1; CLS row/column, padding rows and
+// SLA_SLOT_NONE become n_slots, key columns past the end n_slots + 1) and
+// writes one "needs lookup" flag per tile.  One
 // thread block per tile; every byte of the used tiles and flags is written.
 __global__ void pack_slots_kernel(const uint8_t* __restrict__ slots, int64_t patch_count, int32_t n_slots,
                                   int64_t n_kt, uint8_t* __restrict__ packed, uint8_t* __restrict__ flags) {
   const int64_t tile = blockIdx.x;
   const int64_t qt = tile / n_kt, kt = tile % n_kt;
   uint8_t* dst = packed + tile * intp::kSlotTileBytes;
-  int any = 0;
+  __shared__ uint32_t bits;  // bit w: rows 32w..32w+31 of the tile need the lookup
+  if (threadIdx.x == 0) bits = 0;
+  __syncthreads();
+  uint32_t mine = 0;
   for (int e = threadIdx.x; e < intp::kSlotTileBytes; e += blockDim.x) {
     const int chunk = e / 2048, r = (e % 2048) / 16, c16 = e % 16;
     const int64_t i = qt * intp::kSlotTileQ + r;           // query token
     const int64_t j = kt * intp::kSlotTileK + chunk * 16 + c16;  // key token
     uint8_t v = static_cast<uint8_t>(n_slots);
-    if (i >= 1 && j >= 1 && i <= patch_count && j <= patch_count) {
+    if (j > patch_count) {
+      v = static_cast<uint8_t>(n_slots + 1);  // key past the sequence end: looked up as -inf
+      mine |= 0xFu;
+    } else if (i >= 1 && j >= 1 && i <= patch_count) {
       const uint8_t s = slots[(i - 1) * patch_count + (j - 1)];
       if (s != SLA_SLOT_NONE && s < n_slots) {
         v = s;
-        any = 1;
+        mine |= 1u << (r / 32);
       }
     }
     dst[e] = v;
   }
-  any = __syncthreads_or(any);
-  if (threadIdx.x == 0) flags[tile] = any ? 1 : 0;
+  if (mine) atomicOr(&bits, mine);
+  __syncthreads();
+  if (threadIdx.x == 0) flags[tile] = static_cast<uint8_t>(bits);
 }
 
 }  // namespace
@@ -103,7 +111,7 @@ extern "C" INTP_API intp_status sla_forward_noalloc(const sla_forward_args* a, c
     return INTP_ERR_UNSUPPORTED;
   if (a->seq < 2 || a->batch < 0 || a->heads < 0) return INTP_ERR_SHAPE;
   if (a->seq > kMaxSeq) return INTP_ERR_UNSUPPORTED;  // beyond the scratch capacity
-  if (a->poses < 1 || a->poses > 254 || !a->pose) return INTP_ERR_ARGUMENT;
+  if (a->poses < 1 || a->poses > 253 || !a->pose) return INTP_ERR_ARGUMENT;
   if (a->batch == 0 || a->heads == 0) return INTP_OK;
   const DeviceScratch* d = scratch_for_current_device();
   if (!d) return INTP_ERR_ARCH;

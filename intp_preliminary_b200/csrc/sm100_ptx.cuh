@@ -66,15 +66,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `hint_ns` nanoseconds pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false when
 // the wall-clock budget runs out or when *abort becomes non-zero (another role
 // of the CTA already gave up); on timeout it raises *abort and records `code`.
+// Waiting threads sleep inside try_wait (suspend hint) and look at the clock
+// and the abort flag only between sleeps, so a wait costs few issue slots.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
                                           int32_t* status, int32_t code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
     if (*abort) return false;
     if (global_ns() - start > kWaitBudgetNs) {
       *abort = 1;
@@ -82,6 +98,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       return false;
     }
   }
+}
+
+// Makes this thread's earlier generic-proxy shared-memory writes visible to the
+// async proxy (TMA, tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- TMA

@@ -49,8 +49,8 @@ class LookSlots:
         table = slots.detach().cpu().numpy() if isinstance(slots, torch.Tensor) else np.asarray(slots)
         if table.ndim != 2 or table.shape[0] != table.shape[1]:
             raise ValueError("slots must be a square (Np, Np) table")
-        if not 1 <= int(n_slots) <= 254:
-            raise ValueError("n_slots must be in [1, 254]")
+        if not 1 <= int(n_slots) <= 253:
+            raise ValueError("n_slots must be in [1, 253]")
         table = np.ascontiguousarray(table.astype(np.uint8))
         used = table[table != _lib.SLA_SLOT_NONE]
         if used.size and int(used.max()) >= int(n_slots):

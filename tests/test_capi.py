@@ -70,6 +70,13 @@ def test_pack_slot_table_layout():
             else:
                 assert value == table[i - 1, j - 1]
     assert flags.sum() > 0
+    # keys past the sequence end carry n_slots + 1 (masked); their tile is flagged
+    for qt in range((seq + 127) // 128):
+        kt = nkt - 1
+        for c in range(seq % 64, 64):
+            for r in (0, 77, 127):
+                assert packed[(qt * nkt + kt) * 8192 + (c // 16) * 2048 + r * 16 + c % 16] == 21
+        assert flags[qt * nkt + kt] == 0xF
 
 
 def test_pack_rejects_out_of_range_slot():

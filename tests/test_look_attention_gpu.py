@@ -100,7 +100,9 @@ def test_tcgen05_slots_vs_oracle(cuda_device, dtype, rows, cols):
                                               scale=0.125, return_lse=True)
     err = np.abs(out.float().cpu().numpy() - exact).max()
     assert err <= (8e-3 if dtype == torch.bfloat16 else 2e-3), err
-    assert np.abs(lse.cpu().numpy() - exact_lse).max() <= 1e-4
+    # The tensor-core path sums the 16-bit probabilities it multiplies into V
+    # (row sum accumulated by the PV MMA), so the LSE carries their rounding.
+    assert np.abs(lse.cpu().numpy() - exact_lse).max() <= (4e-3 if dtype == torch.bfloat16 else 1e-3)
     simt, _ = look_attention_forward(q, k, v, pose, look, scale=0.125, kernel="simt")
     assert (out.float() - simt.float()).abs().max().item() <= 1e-2
 
