@@ -1,19 +1,22 @@
-"""Benchmark of the B200 structured Look attention (and companion workloads).
+"""Benchmark of the B200 SHARE-ViT Look-attention path.
 
-Default workload (one step = one Look-attention forward over one batch):
-  look_cfg4   B=64, H=6, N=1025 (CLS + 32x32 offset-row hex lattice), D=64,
-              bf16, Look field 8 directions x 4 rings per (batch, head, query),
-              Q/K/V ~ N(0,1)/8, field ~ U(-1,1)  -> metric: Look-attn TFLOP/s
+Default workload (``--workload model``, BASELINE configs 2 and 5): one step is
+the full half6d3r SHARE-ViT DeiT-Tiny inference forward over 256 images per GPU
+(bf16, random-init weights, images ~ N(0, 1) 224x224x3), plus the gather of
+the logits to rank 0 when N > 1 (weak scaling: 256 images per GPU).  Metric:
+images/s over all GPUs.  The line also carries the Look-attention kernel timed
+in place inside that forward (``roofline``) and BASELINE config 4 (B64 H6
+N1025 D64 bf16) timed on its own (``look_attention_cfg4``).
 
-Other workloads (--workload): look_cfg1 (B8 H3 N197 fp32, 12x4 field),
-negative_l1 (M=256*196, P=576, F=1728 fp32).
+Other workloads: ``look_cfg4`` / ``look_cfg1`` (one Look-attention forward per
+step, TFLOP/s) and ``negative_l1`` (M=256*196, P=576, F=1728 fp32).
 
 Contract: ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``;
-for N>1 launch one process per GPU with torchrun.  Each rank runs the full
-per-GPU workload (weak scaling, no collective on the data path); rank 0
-prints one JSON line.  Timing: CUDA events on the launching stream around
-every step, L2 flushed (256 MiB write) between steps outside the events,
-barrier + synchronize on both sides of the timed loop, max over ranks.
+for N > 1 launch one process per GPU with torchrun.  Timing: CUDA events on the
+launching stream around every step, L2 flushed (256 MiB write) between steps
+outside the events, barrier + synchronize on both sides of the timed loop, max
+over ranks; rank 0 prints one JSON line.  ``--impl reference`` times the
+reference's CPU algorithm (the oracle port) on bounded samples, rank 0 only.
 """
 
 from __future__ import annotations
@@ -29,15 +32,18 @@ import tempfile
 import time
 from pathlib import Path
 
-import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 # DRAM bytes (read + write) of one sla_tc_kernel launch at look_cfg4, from the
-# ncu capture summarised in profiles/look_attention_cfg4_tc.md (None = not captured).
-CFG4_TRAFFIC_BYTES = None
+# ncu capture summarised in profiles/look_attention_cfg4_tc.md.
+CFG4_TRAFFIC_BYTES = int((202.120704 + 33.865216) * 1e6)
+# Algorithmic FLOPs of one half6d3r image (trunk linears, Look attention QK/PV,
+# tokenizer + Look-bank GEMMs), see DESIGN.md.
+MODEL_FLOPS_PER_IMAGE = (196 * 12 * 2 * (192 * 576 + 192 * 192 + 2 * 192 * 768)
+                         + 12 * 4 * 3 * 196 * 196 * 64 + 2 * 195 * (1344 + 336) * 792)
 
 
 def _peaks() -> dict:
@@ -56,7 +62,7 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: str):
         self.gpu_index = gpu_index
         self.proc = None
         self.path = None
@@ -95,15 +101,88 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
         sm = [float(r[1]) for r in rows]
+        power = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+                "samples": len(rows), "power_w_max": max(power) if power else None}
 
 
 # --------------------------------------------------------------------------- workloads
+class ModelWorkload:
+    """Full half6d3r forward over a per-GPU batch; logits gathered to rank 0."""
+
+    name = "model"
+    dtype = torch.bfloat16
+    unit = "images/s"
+    metric = "half6d3r SHARE-ViT DeiT-Tiny inference images/s (bf16)"
+
+    def __init__(self, ctx, per_gpu_batch: int, seed: int):
+        from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+
+        self.ctx = ctx
+        self.device = ctx.device
+        self.batch = per_gpu_batch
+        self.global_batch = per_gpu_batch * ctx.world
+        self.model = ShareViTHalf6d3r(precision="bf16").init_weights(seed=0, look_grid_std=0.02).to(self.device)
+        g = torch.Generator(device=self.device).manual_seed(seed + ctx.rank)
+        self.images = torch.randn(self.batch, 3, 224, 224, device=self.device, generator=g)
+        self.logits = None
+        self.model(self.images[:2])  # build the rendered-prototype cache and the packed slot table
+
+    @property
+    def units_per_step(self) -> float:
+        return float(self.global_batch)
+
+    @property
+    def config(self) -> dict:
+        return {"workload": f"model: half6d3r SHARE-ViT DeiT-Tiny forward, {self.batch} images of 224x224x3 per GPU, "
+                            "bf16, 12 blocks x 3 heads, head_dim 64, 12x4 Look field per layer/head",
+                "batch_per_gpu": self.batch, "global_batch": self.global_batch, "tokens": 196,
+                "look_slots": self.model.look_slots.n_slots}
+
+    def step(self):
+        from intp_preliminary_b200.sharding import gather_to_main
+
+        local = self.model(self.images)
+        self.logits = gather_to_main(local, self.ctx, self.global_batch)
+
+    def e2e_inputs(self):
+        return [self.images.cpu().pin_memory()]
+
+    def e2e_output(self):
+        return torch.empty(self.global_batch if self.ctx.is_main else 1, 100, dtype=torch.float32).pin_memory()
+
+    def e2e_step(self, host_inputs, host_out):
+        from intp_preliminary_b200.sharding import gather_to_main
+
+        images = host_inputs[0].to(self.device, non_blocking=True)
+        logits = gather_to_main(self.model(images), self.ctx, self.global_batch)
+        if logits is not None:
+            host_out.copy_(logits.float(), non_blocking=True)
+
+    def cpu_reference(self):
+        from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+        from oracle.share_vit_cpu import reference_forward_cpu
+
+        cpu_model = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.02)
+        images = self.images[:2].float().cpu()
+        reference_forward_cpu(cpu_model, images)
+        times, t_end = [], time.perf_counter() + 15.0
+        while time.perf_counter() < t_end or len(times) < 2:
+            t0 = time.perf_counter()
+            reference_forward_cpu(cpu_model, images)
+            times.append(time.perf_counter() - t0)
+            if len(times) >= 20:
+                break
+        return 2 / statistics.median(times), f"reference CPU algorithm (dense fields + explicit oracle), 2 images, median of {len(times)}"
+
+
 class LookWorkload:
     """One Look-attention forward over a batch of synthetic inputs."""
 
-    def __init__(self, name: str, device: torch.device, seed: int):
+    unit = "TFLOP/s"
+    metric = "Look-attn TFLOP/s (algorithmic 4*B*H*N^2*D)"
+
+    def __init__(self, name: str, device: torch.device, seed: int, world: int = 1):
         from intp_preliminary_b200 import LookSlots, hexgrid
 
         if name == "look_cfg4":
@@ -112,7 +191,7 @@ class LookWorkload:
             self.batch, self.heads, rows, cols, self.n_dir, self.dtype = 8, 3, 14, 14, 12, torch.float32
         else:
             raise ValueError(name)
-        self.name, self.rows, self.cols, self.n_rad, self.dim = name, rows, cols, 4, 64
+        self.name, self.rows, self.cols, self.n_rad, self.dim, self.world = name, rows, cols, 4, 64, world
         self.patches = rows * cols
         self.seq = self.patches + 1
         self.n_slots = self.n_dir * self.n_rad
@@ -132,6 +211,10 @@ class LookWorkload:
         return 4.0 * self.batch * self.heads * self.seq * self.seq * self.dim
 
     @property
+    def units_per_step(self) -> float:
+        return self.flops * self.world / 1e12
+
+    @property
     def config(self) -> dict:
         return {"workload": f"{self.name}: Look attention B{self.batch} H{self.heads} N{self.seq} D{self.dim} "
                             f"{str(self.dtype).split('.')[-1]}, {self.n_dir}x{self.n_rad} Look field "
@@ -144,52 +227,58 @@ class LookWorkload:
 
         look_attention_forward(self.q, self.k, self.v, self.pose, self.slots, scale=self.scale, out=self.out)
 
-    def input_tensors(self):
-        return [self.q, self.k, self.v, self.pose]
+    def e2e_inputs(self):
+        return [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.pose)]
+
+    def e2e_output(self):
+        return torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
 
     def e2e_step(self, host_inputs, host_out):
-        """Public API with host buffers: H2D copies, forward, D2H of the result."""
         from intp_preliminary_b200 import structured_look_attention
 
         q, k, v, pose = (h.to(self.device, non_blocking=True) for h in host_inputs)
-        out = structured_look_attention(q, k, v, pose, self.slots, scale=self.scale)
-        host_out.copy_(out, non_blocking=True)
+        host_out.copy_(structured_look_attention(q, k, v, pose, self.slots, scale=self.scale), non_blocking=True)
 
-    def cpu_reference(self, sample_batch: int = 1, sample_heads: int = 1) -> tuple[float, str]:
-        """Time the oracle (the reference's CPU algorithm: one-hot fields einsum) on a sample."""
+    def cpu_reference(self, sample_batch: int = 1, sample_heads: int = 1):
         from oracle.look_attention import onehot_fields, reference_structured_look_attention
 
         b, h = sample_batch, sample_heads
         q, k, v = (t[:b, :h].float().cpu().to(self.dtype) for t in (self.q, self.k, self.v))
         pose = self.pose[:b, :, :h].cpu()
         fields = torch.from_numpy(onehot_fields(self.slots_table, self.n_slots, h))
-        reference_structured_look_attention(q, k, v, pose, fields, scale=self.scale)  # warm
-        times = []
-        t_end = time.perf_counter() + 10.0
+        reference_structured_look_attention(q, k, v, pose, fields, scale=self.scale)
+        times, t_end = [], time.perf_counter() + 10.0
         while time.perf_counter() < t_end or len(times) < 3:
             t0 = time.perf_counter()
             reference_structured_look_attention(q, k, v, pose, fields, scale=self.scale)
             times.append(time.perf_counter() - t0)
             if len(times) >= 50:
                 break
-        t = statistics.median(times)
         flops = 4.0 * b * h * self.seq * self.seq * self.dim
-        return flops / t / 1e12, f"B{b} H{h} slice of {self.name}, median of {len(times)} runs"
+        return flops / statistics.median(times) / 1e12, f"B{b} H{h} slice of {self.name}, median of {len(times)} runs"
 
 
 class NegativeL1Workload:
-    def __init__(self, device: torch.device, seed: int, features: int = 1728):
+    unit = "TFLOP/s"
+    metric = "negative-L1 FP32 op/s (2*M*P*F)"
+    dtype = torch.float32
+    name = "negative_l1"
+
+    def __init__(self, device: torch.device, seed: int, world: int = 1, features: int = 1728):
         g = torch.Generator(device=device).manual_seed(seed)
-        self.rows, self.protos, self.features = 256 * 196, 576, features
+        self.rows, self.protos, self.features, self.world = 256 * 196, 576, features, world
         self.x = torch.randn(self.rows, features, device=device, generator=g)
         self.w = torch.randn(self.protos, features, device=device, generator=g) * 0.5
         self.out = torch.empty(self.rows, self.protos, device=device)
         self.device = device
-        self.dtype = torch.float32
 
     @property
     def flops(self) -> float:  # one subtract + one |.|-add per (m, p, f)
         return 2.0 * self.rows * self.protos * self.features
+
+    @property
+    def units_per_step(self) -> float:
+        return self.flops * self.world / 1e12
 
     @property
     def bytes(self) -> float:
@@ -205,8 +294,11 @@ class NegativeL1Workload:
 
         negative_l1_forward(self.x, self.w, out=self.out)
 
-    def input_tensors(self):
-        return [self.x, self.w]
+    def e2e_inputs(self):
+        return [self.x.cpu().pin_memory(), self.w.cpu().pin_memory()]
+
+    def e2e_output(self):
+        return torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
 
     def e2e_step(self, host_inputs, host_out):
         from intp_preliminary_b200 import negative_l1_distance
@@ -214,179 +306,197 @@ class NegativeL1Workload:
         x, w = (h.to(self.device, non_blocking=True) for h in host_inputs)
         host_out.copy_(negative_l1_distance(x, w), non_blocking=True)
 
-    def cpu_reference(self) -> tuple[float, str]:
+    def cpu_reference(self):
         from oracle.negative_l1 import negative_l1_torch
 
         rows = 2048
         x, w = self.x[:rows].cpu(), self.w.cpu()
         negative_l1_torch(x, w)
-        times = []
-        t_end = time.perf_counter() + 10.0
+        times, t_end = [], time.perf_counter() + 10.0
         while time.perf_counter() < t_end or len(times) < 3:
             t0 = time.perf_counter()
             negative_l1_torch(x, w)
             times.append(time.perf_counter() - t0)
-        t = statistics.median(times)
-        return 2.0 * rows * self.protos * self.features / t / 1e12, f"{rows} rows of negative_l1, -cdist p=1"
+        return 2.0 * rows * self.protos * self.features / statistics.median(times) / 1e12, \
+            f"{rows} rows of negative_l1, -cdist p=1"
 
 
 # --------------------------------------------------------------------------- timing
-def _dist_setup(n_gpus: int):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != n_gpus:
-        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    if world > 1:
-        import datetime
+def _timed_steps(step, steps: int, warmup: int, ctx, flush: torch.Tensor) -> list[float]:
+    from intp_preliminary_b200.sharding import barrier
 
-        torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-    return rank, world, local
-
-
-def _barrier(world: int):
-    if world > 1:
-        torch.distributed.barrier()
-
-
-def _max_over_ranks(value: float, world: int, device) -> float:
-    if world == 1:
-        return value
-    t = torch.tensor([value], dtype=torch.float64, device=device)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
-
-
-def _timed_steps(step, steps: int, warmup: int, world: int, device, flush: torch.Tensor) -> list[float]:
-    stream = torch.cuda.current_stream(device)
+    stream = torch.cuda.current_stream(ctx.device)
     for _ in range(warmup):
         step()
-    torch.cuda.synchronize(device)
+    torch.cuda.synchronize(ctx.device)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    _barrier(world)
-    torch.cuda.synchronize(device)
+    barrier(ctx)
+    torch.cuda.synchronize(ctx.device)
     for i in range(steps):
         flush.fill_(i & 0xFF)  # 256 MiB write: evicts inputs from the 126 MB L2
         starts[i].record(stream)
         step()
         ends[i].record(stream)
-    torch.cuda.synchronize(device)
-    _barrier(world)
+    torch.cuda.synchronize(ctx.device)
+    barrier(ctx)
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
-def run_ours(args) -> None:
-    rank, world, local = _dist_setup(args.gpus)
-    device = torch.device("cuda", local if world > 1 else 0)
-    from intp_preliminary_b200 import check_device_status
+def _look_roofline(flops: float, per_launch_ms: float, peaks: dict, traffic, kernel: str, where: str) -> dict:
+    achieved = flops / (per_launch_ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / peaks["bf16_tflops"], 4),
+            "peak_source": f"{peaks['source']} bf16 dense (burst)", "traffic": traffic, "kernel": kernel,
+            "launch_ms": round(per_launch_ms, 5), "where": where}
 
-    if args.workload.startswith("look"):
-        work = LookWorkload(args.workload, device, seed=1234 + rank)
+
+def run_ours(args) -> None:
+    from intp_preliminary_b200 import check_device_status
+    from intp_preliminary_b200.sharding import init_from_env, max_over_ranks, shutdown
+
+    ctx = init_from_env("nccl")
+    if ctx.world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ctx.world}; launch N>1 with torchrun")
+    device = ctx.device
+    peaks = _peaks()
+    if args.workload == "model":
+        work = ModelWorkload(ctx, args.batch, seed=1234)
+    elif args.workload.startswith("look"):
+        work = LookWorkload(args.workload, device, seed=1234 + ctx.rank, world=ctx.world)
     else:
-        work = NegativeL1Workload(device, seed=1234 + rank)
+        work = NegativeL1Workload(device, seed=1234 + ctx.rank, world=ctx.world)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    gpu_index = visible[local] if local < len(visible) else str(local)
+    gpu_index = visible[ctx.local_rank] if ctx.local_rank < len(visible) else str(ctx.local_rank)
+
+    attention_events = []
+    if isinstance(work, ModelWorkload):
+        work.model.attention_events = attention_events
     with ClockSampler(gpu_index) as clocks:
-        times = _timed_steps(work.step, args.steps, args.warmup, world, device, flush)
+        times = _timed_steps(work.step, args.steps, args.warmup, ctx, flush)
     check_device_status(device)
-    total_ms = _max_over_ranks(sum(times), world, device)
+    total_ms = max_over_ranks(sum(times), ctx)
     ms_per_step = total_ms / args.steps
-    peaks = _peaks()
+    value = work.units_per_step * args.steps / (total_ms * 1e-3)
     per_launch_ms = statistics.mean(times)
-    if isinstance(work, LookWorkload):
-        value = work.flops * world * args.steps / (total_ms * 1e-3) / 1e12
-        unit, metric = "TFLOP/s", "Look-attn TFLOP/s (algorithmic 4*B*H*N^2*D)"
-        achieved = work.flops / (per_launch_ms * 1e-3) / 1e12
-        roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
-                    "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                    "peak_source": f"{peaks['source']} bf16 dense (burst, kernel timed alone)",
-                    "traffic": CFG4_TRAFFIC_BYTES if work.name == "look_cfg4" else None,
-                    "kernel": "sla_tc_kernel" if work.dtype != torch.float32 else "sla_simt_kernel"}
+
+    extra = {}
+    if isinstance(work, ModelWorkload):
+        work.model.attention_events = None
+        timed = attention_events[-12 * args.steps:]  # launches inside the timed steps
+        attn_ms = statistics.mean(s.elapsed_time(e) for s, e in timed)
+        flops = 4.0 * args.batch * 3 * 196 * 196 * 64
+        roofline = _look_roofline(flops, attn_ms, peaks, None, "sla_tc_kernel",
+                                  "Look attention inside the model forward (B256 H3 N196 D64 bf16, 68 slots), "
+                                  "CUDA events around each of the 12 launches per timed step")
+        launches = 12 * args.steps
+        # BASELINE config 4 on its own (the N >= 1025 kernel target)
+        cfg4 = LookWorkload("look_cfg4", device, seed=99 + ctx.rank)
+        cfg4_times = _timed_steps(cfg4.step, max(args.steps, 5), args.warmup, ctx, flush)
+        cfg4_ms = max_over_ranks(statistics.mean(cfg4_times), ctx)
+        extra["look_attention_cfg4"] = {
+            "config": cfg4.config["workload"], "tflops": round(cfg4.flops / (cfg4_ms * 1e-3) / 1e12, 2),
+            "roofline": _look_roofline(cfg4.flops, cfg4_ms, peaks, CFG4_TRAFFIC_BYTES, "sla_tc_kernel",
+                                       "BASELINE config 4 timed alone, one launch per step")}
+        extra["model_flops_per_image"] = MODEL_FLOPS_PER_IMAGE
+        extra["model_tflops"] = round(value * MODEL_FLOPS_PER_IMAGE / 1e12, 2)
+    elif isinstance(work, LookWorkload):
+        roofline = _look_roofline(work.flops, per_launch_ms, peaks,
+                                  CFG4_TRAFFIC_BYTES if work.name == "look_cfg4" else None,
+                                  "sla_tc_kernel" if work.dtype != torch.float32 else "sla_simt_kernel",
+                                  "one launch per timed step")
+        launches = args.steps
     else:
-        value = work.flops * world * args.steps / (total_ms * 1e-3) / 1e12
-        unit, metric = "TFLOP/s", "negative-L1 FP32 op/s (2*M*P*F)"
         gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "nl1_kernel",
-                    "note": "FP32-issue bound; see fp32 fraction",
+                    "note": "FP32-issue bound; fp32_tops is the op rate",
                     "fp32_tops": round(work.flops / (per_launch_ms * 1e-3) / 1e12, 2)}
+        launches = args.steps
 
     # End-to-end through the public API with pinned host buffers.
-    host_inputs = [t.cpu().pin_memory() for t in work.input_tensors()]
-    out_shape = work.out.shape
-    host_out = torch.empty(out_shape, dtype=work.out.dtype).pin_memory()
-    e2e_times = _timed_steps(lambda: work.e2e_step(host_inputs, host_out), args.steps, args.warmup, world, device,
-                             flush)
-    e2e_total = _max_over_ranks(sum(e2e_times), world, device)
-    e2e_value = work.flops * world * args.steps / (e2e_total * 1e-3) / 1e12
+    host_inputs = work.e2e_inputs()
+    host_out = work.e2e_output()
+    e2e_times = _timed_steps(lambda: work.e2e_step(host_inputs, host_out), args.steps, args.warmup, ctx, flush)
+    e2e_total = max_over_ranks(sum(e2e_times), ctx)
+    e2e_value = work.units_per_step * args.steps / (e2e_total * 1e-3)
     h2d = sum(t.numel() * t.element_size() for t in host_inputs)
-    d2h = host_out.numel() * host_out.element_size()
+    d2h = host_out.numel() * host_out.element_size() if ctx.is_main else 0
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if ctx.is_main and not args.no_cpu_baseline:
         cpu_value, sample = work.cpu_reference()
-        cpu = {"value": round(cpu_value, 6), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+        cpu = {"value": round(cpu_value, 6), "unit": work.unit, "cores": torch.get_num_threads(), "kind": "port",
                "sample": sample}
-    if rank == 0:
+    if ctx.is_main:
         line = {
-            "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "metric": work.metric, "value": round(value, 3), "unit": work.unit, "n_gpus": ctx.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": {torch.bfloat16: "bf16", torch.float32: "f32"}[work.dtype],
-            "data": "synthetic (seeded; BASELINE shapes and distributions)",
-            "config": {**work.config, "parallelism": f"independent replicas x{world} (weak)",
+            "data": "synthetic (seeded; BASELINE shapes and distributions, random-init weights)",
+            "config": {**work.config,
+                       "parallelism": f"batch-sharded replicas x{ctx.world} (weak), logits gathered to rank 0"
+                       if isinstance(work, ModelWorkload) else f"independent replicas x{ctx.world} (weak)",
                        "l2": "flushed between steps (256 MiB write outside the timed events)"},
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 4), "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps,
+            "e2e": {"value": round(e2e_value, 4), "unit": work.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
             "clocks": clocks.summary(),
+            **extra,
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    shutdown(ctx)
 
 
 def run_reference(args) -> None:
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """The reference's CPU algorithm on bounded samples of the same workload (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    device = torch.device("cpu")
-    if args.workload.startswith("look"):
+    if args.workload == "model":
+        from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+        from oracle.share_vit_cpu import reference_forward_cpu
+
+        model = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.02)
+        images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(1234))
+        step = lambda: reference_forward_cpu(model, images)  # noqa: E731
+        units, unit = 2.0, "images/s"
+        metric = ModelWorkload.metric
+        config = {"workload": f"model: half6d3r SHARE-ViT DeiT-Tiny forward, {args.batch} images per GPU",
+                  "batch_per_gpu": args.batch}
+        sample = "2 images per step through the reference CPU algorithm (dense fields + explicit oracle)"
+        dtype = "f32"
+    elif args.workload.startswith("look"):
         work = _CpuLook(args.workload)
+        step, units, unit = work.step, work.sample_flops / 1e12, "TFLOP/s"
+        metric, config, sample, dtype = LookWorkload.metric, work.config, work.sample, work.dtype_name
     else:
-        raise SystemExit("reference arm implemented for the Look workloads")
+        raise SystemExit("reference arm: model or look workloads")
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        work.step()
-        dt = time.perf_counter() - t0
+        step()
         if i >= args.warmup:
-            times.append(dt)
-    value = work.sample_flops * len(times) / sum(times) / 1e12
-    line = {
-        "impl": "reference", "metric": "Look-attn TFLOP/s (algorithmic 4*B*H*N^2*D)", "value": round(value, 6),
-        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * sum(times) / len(times), 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": work.dtype_name, "data": "synthetic", "config": work.config,
-        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": work.sample},
-        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    del device
+            times.append(time.perf_counter() - t0)
+    value = units * len(times) / sum(times)
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": config,
+        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
 class _CpuLook:
     """The reference's CPU path (oracle port: one-hot fields einsum) on a bounded
-    per-step sample of the Look workload: one (batch, head) slice per step."""
+    per-step sample of a Look workload: one (batch, head) slice per step."""
 
     def __init__(self, name: str):
         from intp_preliminary_b200 import hexgrid
@@ -418,10 +528,11 @@ class _CpuLook:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
-    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["look_cfg4", "look_cfg1", "negative_l1"], default="look_cfg4")
+    parser.add_argument("--workload", choices=["model", "look_cfg4", "look_cfg1", "negative_l1"], default="model")
+    parser.add_argument("--batch", type=int, default=256, help="images per GPU (model workload)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     if args.warmup < 3:

@@ -17,6 +17,11 @@ reference checkout is available, passed as --reference, default
   hex_bins_reference.npz
       ``hex_relative_bins`` (utils/hex_graph.py:25-47) on the synthetic
       14x14 lattice and on the real half6d3r tokenizer lattice (195 patches).
+  share_vit_reference.npz
+      The reference half6d3r ``DeiTTinyRotHexLook`` forward (fp32, CPU) on two
+      seeded images, with the weights of ``ShareViTHalf6d3r.init_weights(seed=0,
+      look_grid_std=0.5)`` loaded into it: logits, CLS features, the first 8
+      patch tokens and Look pose weights.
 
 The slot tables of the synthetic configurations come from the scalar oracle
 restatement (oracle/hex_lattice.py); the reference has no code for that
@@ -141,6 +146,27 @@ def main() -> None:
     hexes["real_rings"] = rings.numpy().astype(np.uint8)
     hexes["real_dirs"] = dirs.numpy().astype(np.uint8)
     np.savez_compressed(HERE / "hex_bins_reference.npz", **hexes)
+
+    # --- full half6d3r model ----------------------------------------------------------
+    # Weights come from the product's seeded init (ShareViTHalf6d3r.init_weights, which
+    # keeps the reference's parameter names), loaded into the reference model; the
+    # images are drawn from a seeded generator, so the GPU-side test regenerates both.
+    from model.deit_tiny_rot_hex_look import DeiTTinyRotHexLook
+    from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+    ours = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.5)
+    ref = DeiTTinyRotHexLook(use_pos_embed=True, directions=6, global_directions=12, angular_bins_per_radius=3,
+                             look_compact_variable_rings=True, tokenizer_null_initial_score=0.0).eval()
+    ref.load_state_dict(ours.state_dict(), strict=True)
+    images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(5))
+    with torch.no_grad():
+        tokens = ref.patch_embed(images)
+        feats = ref.forward_features(images)
+        logits = ref.head(feats[:, 0])
+        rings, coverage = ref.look_bank.extract_rings(images)
+        pose = ref.look_bank.pose_weights(rings, coverage).flatten(-2)
+    np.savez_compressed(HERE / "share_vit_reference.npz", logits=logits.numpy(), cls_features=feats[:, 0].numpy(),
+                        tokens_head=tokens[:, :8].numpy(), pose_head=pose[:, :8].numpy(),
+                        image_seed=np.int64(5), weight_seed=np.int64(0), look_grid_std=np.float64(0.5))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 

@@ -1,0 +1,49 @@
+"""SHARE-ViT half6d3r forward on the GPU kernels against the reference's logits."""
+
+import numpy as np
+import pytest
+import torch
+
+from intp_preliminary_b200 import check_device_status
+from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+from tests.golden_data import load
+
+pytestmark = pytest.mark.gpu
+GOLD = load("share_vit_reference.npz")
+
+
+def _model(precision, device):
+    m = ShareViTHalf6d3r(precision=precision).init_weights(seed=int(GOLD["weight_seed"]),
+                                                           look_grid_std=float(GOLD["look_grid_std"]))
+    return m.to(device)
+
+
+def _images(device):
+    g = torch.Generator().manual_seed(int(GOLD["image_seed"]))
+    return torch.randn(2, 3, 224, 224, generator=g).to(device)
+
+
+def test_fp32_forward_matches_reference(cuda_device):
+    logits = _model("fp32", cuda_device)(_images(cuda_device)).cpu().numpy()
+    check_device_status(cuda_device)
+    np.testing.assert_allclose(logits, GOLD["logits"], atol=1e-4, rtol=1e-4)
+
+
+def test_bf16_forward_tracks_reference(cuda_device):
+    """bf16 GEMMs + tensor-core Look attention vs the fp32 reference."""
+    logits = _model("bf16", cuda_device)(_images(cuda_device)).float().cpu().numpy()
+    check_device_status(cuda_device)
+    ref = GOLD["logits"]
+    err = np.abs(logits - ref).max()
+    assert err <= 0.05 * np.abs(ref).max(), err
+    assert np.corrcoef(logits.ravel(), ref.ravel())[0, 1] > 0.999
+
+
+def test_bf16_batch_forward_is_finite_and_batch_consistent(cuda_device):
+    model = _model("bf16", cuda_device)
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    images = torch.randn(48, 3, 224, 224, device=cuda_device, generator=g)
+    full = model(images)
+    part = model(images[:16])
+    assert torch.isfinite(full).all()
+    assert (full[:16] - part).abs().max().item() <= 1e-2
