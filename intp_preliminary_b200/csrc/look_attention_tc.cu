@@ -43,7 +43,6 @@ constexpr int BN = 64;             // keys per tile
 constexpr int HD = 64;             // head_dim
 constexpr int ON = HD + 16;        // PV MMA N: 64 outputs + the ones block (row sum in column 64)
 constexpr int kThreads = 192;
-constexpr int kKStages = 3;   // K tile + slot tile ring (released after S(j) and the slot reads)
 constexpr int kVStages = 2;   // V tile ring (released after PV(j))
 constexpr uint32_t kQBytes = BM * HD * 2;      // 16 KB
 constexpr uint32_t kKVBytes = BN * HD * 2;     // 8 KB each of K and V (and the ones tile)
@@ -54,10 +53,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 2^8
 constexpr int kMaxSlots = 93;
-
+template <int KS>
 struct alignas(8) Barriers {
   uint64_t q_full, q_empty;
-  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t k_full[KS], k_empty[KS];
   uint64_t v_full[kVStages], v_empty[kVStages];
   // s_full[b]: S of a tile is in buffer b.  p_full[b]: its P is stored there.
   // pv_done[b]: the PV that read that P finished (buffer b is free again).
@@ -68,14 +67,17 @@ struct alignas(8) Barriers {
   int32_t abort;
 };
 
+// KS = stages of the K / slot-tile ring: 3 normally, 2 when the per-query
+// Look table is large (keeps two CTAs per SM).
+template <int KS>
 struct SmemLayout {
   // offsets relative to a 1024-byte aligned base
   static constexpr uint32_t q = 0;
   static constexpr uint32_t k = q + kQBytes;
-  static constexpr uint32_t v = k + kKStages * kKVBytes;
+  static constexpr uint32_t v = k + KS * kKVBytes;
   static constexpr uint32_t ones = v + kVStages * kKVBytes;  // constant [keys][64] tile, column 0 = 1
   static constexpr uint32_t slots = ones + kKVBytes;
-  static constexpr uint32_t table = slots + kKStages * kSlotBytes;
+  static constexpr uint32_t table = slots + KS * kSlotBytes;
 };
 
 __device__ __forceinline__ float load_any(const void* p, int64_t idx, int32_t dtype) {
@@ -114,9 +116,25 @@ __device__ __forceinline__ float row_max64(const float2 (&t)[32]) {
   return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
 }
 
-__device__ __forceinline__ uint32_t pack_out(uint32_t lo, uint32_t hi, float inv, int32_t dtype) {
-  const float a = __uint_as_float(lo) * inv, b = __uint_as_float(hi) * inv;
-  return dtype == 2 ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_out(uint32_t lo, uint32_t hi, float inv) {
+  return pack2<BF16>(__uint_as_float(lo) * inv, __uint_as_float(hi) * inv);
+}
+
+// P = 2^(t * cs - m) for the 64 keys of a row, packed to 16-bit pairs in key order.
+template <bool BF16>
+__device__ __forceinline__ void exp_pack(const float2 (&t)[BN / 2], float cs, float m, uint32_t (&w)[BN / 2]) {
+  const float2 c2 = make_float2(cs, cs), nm2 = make_float2(-m, -m);
+#pragma unroll
+  for (int c = 0; c < BN / 2; ++c) {
+    const float2 x = fma2(t[c], c2, nm2);
+    w[c] = pack2<BF16>(fast_exp2(x.x), fast_exp2(x.y));
+  }
 }
 
 struct TcArgs {
@@ -128,21 +146,23 @@ struct TcArgs {
   int32_t pose_vec4;      // pose rows are 16-byte aligned fp32 with unit slot stride
 };
 
+template <int KS, bool BF16>
 __global__ void __launch_bounds__(kThreads, 2)
 sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
+  using Layout = SmemLayout<KS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment (128B-swizzle tiles) by an offset from the __shared__
   // array itself, so every derived pointer stays in the shared address space
   // (32-bit LDS/STS instead of generic 64-bit loads).
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + SmemLayout::table + a.table_bytes);
-  uint8_t* q_s = smem + SmemLayout::q;
-  uint8_t* k_s = smem + SmemLayout::k;
-  uint8_t* v_s = smem + SmemLayout::v;
-  uint8_t* ones_s = smem + SmemLayout::ones;
-  uint8_t* slot_s = smem + SmemLayout::slots;
-  float* table_s = reinterpret_cast<float*>(smem + SmemLayout::table);
+  Barriers<KS>* bars = reinterpret_cast<Barriers<KS>*>(smem + Layout::table + a.table_bytes);
+  uint8_t* q_s = smem + Layout::q;
+  uint8_t* k_s = smem + Layout::k;
+  uint8_t* v_s = smem + Layout::v;
+  uint8_t* ones_s = smem + Layout::ones;
+  uint8_t* slot_s = smem + Layout::slots;
+  float* table_s = reinterpret_cast<float*>(smem + Layout::table);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -152,7 +172,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->q_empty, 1);
-    for (int s = 0; s < kKStages; ++s) {
+    for (int s = 0; s < KS; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1 + 4);  // S-MMA commit + 4 softmax warps (slot reads)
     }
@@ -172,7 +192,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   // The ones tile: a 64-key x 64-column bf16/f16 block in the same 128B-swizzled
   // layout TMA gives V, with logical column 0 equal to 1 and every other column 0.
   if (warp < 4) {
-    const uint16_t one = p.dtype == 2 ? uint16_t(0x3F80) : uint16_t(0x3C00);
+    const uint16_t one = BF16 ? uint16_t(0x3F80) : uint16_t(0x3C00);
     for (int w = threadIdx.x; w < static_cast<int>(kKVBytes / 16); w += 128) {
       const int r = w >> 3, chunk = w & 7;  // 16-byte chunk `chunk` of key row r
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -190,14 +210,16 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
+  // Work-item indices fit 32 bits (checked on the host): 32-bit divisions.
   const int64_t N = p.seq;
-  const int64_t H = p.heads;
+  const uint32_t H = static_cast<uint32_t>(p.heads);
   const int64_t n_kt = a.n_kt;
+  const uint32_t n_qt = static_cast<uint32_t>(a.n_qt), n_items = static_cast<uint32_t>(a.n_items);
   const bool use_bias = a.n_slots > 0;
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
-    // K tiles (with their slot tiles) run up to kKStages ahead; V tiles lag one
+    // K tiles (with their slot tiles) run up to KS ahead; V tiles lag one
     // key tile behind K so a V stage still in use never blocks the next K load.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -216,9 +238,9 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         ++v_iter;
         return true;
       };
-      for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++item_iter) {
-        const int64_t qt = item % a.n_qt;
-        const int64_t bh = item / a.n_qt;
+      for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_iter) {
+        const uint32_t qt = item % n_qt;
+        const uint32_t bh = item / n_qt;
         const int32_t h = static_cast<int32_t>(bh % H), b = static_cast<int32_t>(bh / H);
         if (item_iter > 0 && !mbar_wait(&bars->q_empty, (item_iter - 1) & 1, abort_flag, p.status,
                                         kDevTimeoutProducer)) {
@@ -232,7 +254,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                       map_coord(a.oq, 3, r, h, b));
         }
         for (int64_t j = 0; j < n_kt; ++j) {
-          const uint32_t ks = k_iter % kKStages, n = k_iter / kKStages;
+          const uint32_t ks = k_iter % KS, n = k_iter / KS;
           if (n > 0 && !mbar_wait(&bars->k_empty[ks], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
@@ -257,8 +279,8 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       // Stage s of a ring with `issued` loads received (issued - s + R - 1) / R of them.
       volatile int32_t no_abort = 0;
       if (item_iter > 0) mbar_wait(&bars->q_full, (item_iter - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
-      for (uint32_t st = 0; st < kKStages; ++st) {
-        const uint32_t cnt = k_iter > st ? (k_iter - st + kKStages - 1) / kKStages : 0;
+      for (uint32_t st = 0; st < KS; ++st) {
+        const uint32_t cnt = k_iter > st ? (k_iter - st + KS - 1) / KS : 0;
         if (cnt > 0) mbar_wait(&bars->k_full[st], (cnt - 1) & 1, &no_abort, p.status, kDevTimeoutDrain);
       }
       for (uint32_t st = 0; st < kVStages; ++st) {
@@ -269,9 +291,8 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const bool bf16 = p.dtype == 2;
-      const uint32_t idesc_qk = idesc_f16(bf16, false, BM, BN);
-      const uint32_t idesc_pv = idesc_f16(bf16, true, BM, ON);
+      const uint32_t idesc_qk = idesc_f16(BF16, false, BM, BN);
+      const uint32_t idesc_pv = idesc_f16(BF16, true, BM, ON);
       // Descriptors are built once; a K step / stage advances only the 14-bit
       // start-address field (16-byte units) in the low word, which cannot carry.
       // V is MN-major with two 64-wide column blocks: the V tile and, LBO bytes
@@ -302,15 +323,15 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         ++v_iter;
         return true;
       };
-      for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++item_iter) {
+      for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_iter) {
         if (!mbar_wait(&bars->q_full, item_iter & 1, abort_flag, p.status, kDevTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int64_t j = 0; j < n_kt && ok; ++j) {
-          const uint32_t ks = k_iter % kKStages;
-          if (!mbar_wait(&bars->k_full[ks], (k_iter / kKStages) & 1, abort_flag, p.status, kDevTimeoutMma)) {
+          const uint32_t ks = k_iter % KS;
+          if (!mbar_wait(&bars->k_full[ks], (k_iter / KS) & 1, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -366,24 +387,34 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       return mbar_wait(&bars->pv_done[t & 1], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax);
     };
     bool ok = true;
-    for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x) {
-      const int64_t qt = item % a.n_qt;
-      const int64_t bh = item / a.n_qt;
+    for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const uint32_t qt = item % n_qt;
+      const uint32_t bh = item / n_qt;
       const int64_t h = bh % H, b = bh / H;
-      const int64_t i = qt * BM + row;  // token index of this thread's row
+      const int64_t i = static_cast<int64_t>(qt) * BM + row;  // token index of this thread's row
       if (use_bias) {
         // Per-query Look values, [slot][row] layout (bank = row % 32: conflict
         // free), pre-scaled to the log2 domain.  Only this thread reads its column.
         const bool valid = i >= 1 && i < N;
         const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
         if (a.pose_vec4) {
+          // Eight 16-byte loads in flight per batch: one memory round trip per 32 slots.
           const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
-          for (int s4 = 0; s4 < ns / 4; ++s4) {
-            const float4 v4 = valid ? __ldg(src + s4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            table_s[(4 * s4 + 0) * BM + row] = v4.x * kLog2e;
-            table_s[(4 * s4 + 1) * BM + row] = v4.y * kLog2e;
-            table_s[(4 * s4 + 2) * BM + row] = v4.z * kLog2e;
-            table_s[(4 * s4 + 3) * BM + row] = v4.w * kLog2e;
+          for (int s0 = 0; s0 < ns / 4; s0 += 8) {
+            float4 v4[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              v4[u] = (valid && s0 + u < ns / 4) ? __ldg(src + s0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              if (s0 + u < ns / 4) {
+                float* dst = table_s + 4 * (s0 + u) * BM + row;
+                dst[0] = v4[u].x * kLog2e;
+                dst[BM] = v4[u].y * kLog2e;
+                dst[2 * BM] = v4[u].z * kLog2e;
+                dst[3 * BM] = v4[u].w * kLog2e;
+              }
+            }
           }
         } else {
           for (int s = 0; s < ns; ++s)
@@ -434,10 +465,10 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
         // t holds raw scores on tiles without Look bias, and the log2-domain
         // logits scale*log2(e)*s + bias on tiles with it.
-        const uint32_t st = k_iter % kKStages;
+        const uint32_t st = k_iter % KS;
         const bool bias_tile = (tile_mask >> (j & 63)) & 1u;
         if (bias_tile) {
-          if (!mbar_wait(&bars->k_full[st], (k_iter / kKStages) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+          if (!mbar_wait(&bars->k_full[st], (k_iter / KS) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
             ok = false;
             break;
           }
@@ -503,20 +534,10 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // Probabilities (log2 domain, relative to the running max), written as
         // 16-bit pairs over the S columns they came from.  The row sum is not
         // kept here: the PV MMA accumulates it into O column 64.
-        const float cs = bias_tile ? 1.f : scale_log2;
-        const float2 c2 = make_float2(cs, cs), nm2 = make_float2(-m, -m);
-        uint32_t w0[16], w1[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float2 x0 = fma2(t[e], c2, nm2);
-          const float2 x1 = fma2(t[16 + e], c2, nm2);
-          const float p0 = fast_exp2(x0.x), p1 = fast_exp2(x0.y);
-          const float p2 = fast_exp2(x1.x), p3 = fast_exp2(x1.y);
-          w0[e] = (p.dtype == 2) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-          w1[e] = (p.dtype == 2) ? pack_bf16x2(p2, p3) : pack_f16x2(p2, p3);
-        }
-        tmem_st16(s_addr, w0);
-        tmem_st16(s_addr + 16, w1);
+        uint32_t w[BN / 2];
+        exp_pack<BF16>(t, bias_tile ? 1.f : scale_log2, m, w);
+        tmem_st16(s_addr, *reinterpret_cast<const uint32_t(*)[16]>(w));
+        tmem_st16(s_addr + 16, *reinterpret_cast<const uint32_t(*)[16]>(w + 16));
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -549,10 +570,10 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const float inv = 1.f / l;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          packed[e] = pack_out(r0[2 * e], r0[2 * e + 1], inv, p.dtype);
-          packed[8 + e] = pack_out(r1[2 * e], r1[2 * e + 1], inv, p.dtype);
-          packed[16 + e] = pack_out(r2[2 * e], r2[2 * e + 1], inv, p.dtype);
-          packed[24 + e] = pack_out(r3[2 * e], r3[2 * e + 1], inv, p.dtype);
+          packed[e] = pack_out<BF16>(r0[2 * e], r0[2 * e + 1], inv);
+          packed[8 + e] = pack_out<BF16>(r1[2 * e], r1[2 * e + 1], inv);
+          packed[16 + e] = pack_out<BF16>(r2[2 * e], r2[2 * e + 1], inv);
+          packed[24 + e] = pack_out<BF16>(r3[2 * e], r3[2 * e + 1], inv);
         }
       }
       tc_fence_before();
@@ -649,11 +670,40 @@ uint32_t table_bytes_for(int32_t n_slots) {
   return n_slots > 0 ? static_cast<uint32_t>((n_slots + 2) * BM * sizeof(float)) : 0u;
 }
 
+template <int KS>
 size_t smem_bytes_for(uint32_t table_bytes) {
-  size_t bytes = 1024 + SmemLayout::table + table_bytes + sizeof(Barriers) + 64;
+  size_t bytes = 1024 + SmemLayout<KS>::table + table_bytes + sizeof(Barriers<KS>) + 64;
   // Keep at most two CTAs per SM so two TMEM allocations of 256 columns fit.
   const size_t floor_bytes = 80 * 1024;
   return bytes < floor_bytes ? floor_bytes : bytes;
+}
+
+// Sets the kernel's shared-memory attributes, works out how many CTAs fit on
+// an SM (at most two: two 256-column TMEM allocations) and launches a
+// persistent grid of that many CTAs per SM.
+template <int KS, bool BF16>
+int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const TcArgs& a,
+                       size_t smem, int smem_per_sm, int regs_per_sm, int sm_count, cudaStream_t stream) {
+  auto kernel = sla_tc_kernel<KS, BF16>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+          cudaSuccess)
+    return 6;
+  // Resident CTAs per SM from the register and shared-memory budgets (the
+  // occupancy query does not account for the carveout set above).
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) return 6;
+  const int warp_regs = ((fa.numRegs * 32 + 255) / 256) * 256;
+  const int by_regs = regs_per_sm / (warp_regs * (kThreads / 32));
+  const int by_smem = smem_per_sm / static_cast<int>(smem + 1024);
+  int per_sm = by_regs < by_smem ? by_regs : by_smem;
+  if (per_sm > 2) per_sm = 2;
+  if (per_sm < 1) return 6;
+  int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
+  if (grid > a.n_items) grid = a.n_items;
+  kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(mq, mk, mv, a);
+  return cudaGetLastError() == cudaSuccess ? 0 : 6;
 }
 
 }  // namespace
@@ -667,6 +717,7 @@ int32_t sla_tc_supported(const SlaParams& p) {
   if (p.status == nullptr) return 0;
   if (p.seq < 2 || p.seq > (int64_t(1) << 30) || p.batch > (int64_t(1) << 30) || p.heads > (int64_t(1) << 30))
     return 0;
+  if (p.batch * p.heads * ((p.seq + BM - 1) / BM) > INT32_MAX) return 0;  // 32-bit work-item indices
   if (!(p.scale > 0.f) || !(p.scale < 3.0e38f)) return 0;
   if (!tma_stride_ok(p.q, p.q_stride) || !tma_stride_ok(p.k, p.k_stride) || !tma_stride_ok(p.v, p.v_stride))
     return 0;
@@ -695,30 +746,20 @@ int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
       reinterpret_cast<uintptr_t>(p.pose) % 16 == 0 && p.pose_stride[0] % 4 == 0 && p.pose_stride[1] % 4 == 0 &&
       p.pose_stride[2] % 4 == 0)
     a.pose_vec4 = 1;
-  const size_t smem = smem_bytes_for(a.table_bytes);
-  if (cudaFuncSetAttribute(sla_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess ||
-      cudaFuncSetAttribute(sla_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-    return 6;
-  // Resident CTAs per SM from the register and shared-memory budgets (the
-  // occupancy query does not account for the carveout set above).
   int dev = 0, smem_per_sm = 0, regs_per_sm = 0;
-  cudaFuncAttributes fa;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaFuncGetAttributes(&fa, sla_tc_kernel) != cudaSuccess ||
+  if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&regs_per_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess)
     return 6;
-  const int warp_regs = ((fa.numRegs * 32 + 255) / 256) * 256;
-  const int by_regs = regs_per_sm / (warp_regs * (kThreads / 32));
-  const int by_smem = smem_per_sm / static_cast<int>(smem + 1024);
-  int per_sm = by_regs < by_smem ? by_regs : by_smem;
-  if (per_sm > 2) per_sm = 2;  // two 256-column TMEM allocations per SM
-  if (per_sm < 1) return 6;
-  int64_t grid = static_cast<int64_t>(sm_count) * per_sm;
-  if (grid > a.n_items) grid = a.n_items;
-  sla_tc_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(mq, mk, mv, a);
-  return cudaGetLastError() == cudaSuccess ? 0 : 6;
+  // Three K / slot-tile stages when two CTAs still fit on an SM, else two.
+  const size_t smem3 = smem_bytes_for<3>(a.table_bytes), smem2 = smem_bytes_for<2>(a.table_bytes);
+  const bool three = 2 * (smem3 + 1024) <= static_cast<size_t>(smem_per_sm);
+  const bool bf16 = p.dtype == 2;
+  if (three)
+    return bf16 ? launch_variant<3, true>(mq, mk, mv, a, smem3, smem_per_sm, regs_per_sm, sm_count, stream)
+                : launch_variant<3, false>(mq, mk, mv, a, smem3, smem_per_sm, regs_per_sm, sm_count, stream);
+  return bf16 ? launch_variant<2, true>(mq, mk, mv, a, smem2, smem_per_sm, regs_per_sm, sm_count, stream)
+              : launch_variant<2, false>(mq, mk, mv, a, smem2, smem_per_sm, regs_per_sm, sm_count, stream);
 }
 
 }  // namespace intp
