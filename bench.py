@@ -127,6 +127,9 @@ class ModelWorkload:
         self.images = torch.randn(self.batch, 3, 224, 224, device=self.device, generator=g)
         self.logits = None
         self.model(self.images[:2])  # build the rendered-prototype cache and the packed slot table
+        from intp_preliminary_b200.serving import GraphedForward
+
+        self.graphed = GraphedForward(self.model, self.images)  # the whole forward as one CUDA graph
 
     @property
     def units_per_step(self) -> float:
@@ -142,22 +145,39 @@ class ModelWorkload:
     def step(self):
         from intp_preliminary_b200.sharding import gather_to_main
 
-        local = self.model(self.images)
+        local = self.graphed.replay()
         self.logits = gather_to_main(local, self.ctx, self.global_batch)
 
+    def eager_step(self):
+        """The same forward launched kernel by kernel (for in-model kernel timing)."""
+        self.model(self.images)
+
     def e2e_inputs(self):
-        return [self.images.cpu().pin_memory()]
+        g = torch.Generator().manual_seed(4321 + self.ctx.rank)
+        return [torch.randn(self.batch, 3, 224, 224, generator=g).pin_memory() for _ in range(2)]
 
     def e2e_output(self):
         return torch.empty(self.global_batch if self.ctx.is_main else 1, 100, dtype=torch.float32).pin_memory()
 
-    def e2e_step(self, host_inputs, host_out):
+    def e2e_run(self, host_inputs, host_out, steps: int) -> float:
+        """`steps` batches from pinned host memory through PipelinedInference
+        (H2D of batch i+1 overlapped with the forward of batch i, logits
+        gathered to rank 0 and copied back every step); device ms in total."""
+        from intp_preliminary_b200.serving import PipelinedInference
         from intp_preliminary_b200.sharding import gather_to_main
 
-        images = host_inputs[0].to(self.device, non_blocking=True)
-        logits = gather_to_main(self.model(images), self.ctx, self.global_batch)
-        if logits is not None:
-            host_out.copy_(logits.float(), non_blocking=True)
+        if not hasattr(self, "pipeline"):
+            self.pipeline = PipelinedInference(self.model, self.batch, self.device)
+        outs = [host_out] * steps
+        batches = [host_inputs[i % len(host_inputs)] for i in range(steps)]
+        gather = lambda i, logits: gather_to_main(logits, self.ctx, self.global_batch)  # noqa: E731
+        stream = torch.cuda.current_stream(self.device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        self.pipeline.run(batches, outs, after_forward=gather)
+        end.record(stream)
+        torch.cuda.synchronize(self.device)
+        return start.elapsed_time(end)
 
     def cpu_reference(self):
         from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
@@ -353,7 +373,7 @@ def _look_roofline(flops: float, per_launch_ms: float, peaks: dict, traffic, ker
 
 def run_ours(args) -> None:
     from intp_preliminary_b200 import check_device_status
-    from intp_preliminary_b200.sharding import init_from_env, max_over_ranks, shutdown
+    from intp_preliminary_b200.sharding import barrier, init_from_env, max_over_ranks, shutdown
 
     ctx = init_from_env("nccl")
     if ctx.world != args.gpus:
@@ -370,9 +390,6 @@ def run_ours(args) -> None:
     visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
     gpu_index = visible[ctx.local_rank] if ctx.local_rank < len(visible) else str(ctx.local_rank)
 
-    attention_events = []
-    if isinstance(work, ModelWorkload):
-        work.model.attention_events = attention_events
     with ClockSampler(gpu_index) as clocks:
         times = _timed_steps(work.step, args.steps, args.warmup, ctx, flush)
     check_device_status(device)
@@ -383,14 +400,20 @@ def run_ours(args) -> None:
 
     extra = {}
     if isinstance(work, ModelWorkload):
+        # The attention kernel in place: the same forward launched eagerly with
+        # CUDA events around each of its 12 Look-attention launches.
+        attention_events = []
+        work.model.attention_events = attention_events
+        _timed_steps(work.eager_step, args.steps, args.warmup, ctx, flush)
         work.model.attention_events = None
-        timed = attention_events[-12 * args.steps:]  # launches inside the timed steps
+        timed = attention_events[-12 * args.steps:]
         attn_ms = statistics.mean(s.elapsed_time(e) for s, e in timed)
         flops = 4.0 * args.batch * 3 * 196 * 196 * 64
         roofline = _look_roofline(flops, attn_ms, peaks, None, "sla_tc_kernel",
                                   "Look attention inside the model forward (B256 H3 N196 D64 bf16, 68 slots), "
-                                  "CUDA events around each of the 12 launches per timed step")
-        launches = 12 * args.steps
+                                  "CUDA events around each of its 12 launches in an eager run of the timed forward")
+        # ours per step: 12 Look attention + hex gather + post-GEMM + 25 add/LayerNorm
+        launches = (12 + 1 + 1 + 25) * args.steps
         # BASELINE config 4 on its own (the N >= 1025 kernel target)
         cfg4 = LookWorkload("look_cfg4", device, seed=99 + ctx.rank)
         cfg4_times = _timed_steps(cfg4.step, max(args.steps, 5), args.warmup, ctx, flush)
@@ -418,10 +441,18 @@ def run_ours(args) -> None:
     # End-to-end through the public API with pinned host buffers.
     host_inputs = work.e2e_inputs()
     host_out = work.e2e_output()
-    e2e_times = _timed_steps(lambda: work.e2e_step(host_inputs, host_out), args.steps, args.warmup, ctx, flush)
-    e2e_total = max_over_ranks(sum(e2e_times), ctx)
+    if isinstance(work, ModelWorkload):
+        # Batches stream from host memory (each step copies its own 154 MB
+        # batch, larger than L2); copies overlap the previous step's forward.
+        work.e2e_run(host_inputs, host_out, args.warmup)
+        barrier(ctx)
+        e2e_total = max_over_ranks(work.e2e_run(host_inputs, host_out, args.steps), ctx)
+        h2d = host_inputs[0].numel() * host_inputs[0].element_size()
+    else:
+        e2e_times = _timed_steps(lambda: work.e2e_step(host_inputs, host_out), args.steps, args.warmup, ctx, flush)
+        e2e_total = max_over_ranks(sum(e2e_times), ctx)
+        h2d = sum(t.numel() * t.element_size() for t in host_inputs)
     e2e_value = work.units_per_step * args.steps / (e2e_total * 1e-3)
-    h2d = sum(t.numel() * t.element_size() for t in host_inputs)
     d2h = host_out.numel() * host_out.element_size() if ctx.is_main else 0
 
     cpu = None

@@ -1,0 +1,79 @@
+/*
+ * intp_share_vit.h - C ABI of the fused steps of the half6d3r SHARE-ViT
+ * forward that surround the Look attention (libintp_b200.so).
+ *
+ * The reference runs these steps as chains of PyTorch operators; each entry
+ * point below replaces one such chain with one kernel:
+ *   svit_gather_patches : HexPatchGeometry's reflect-padded circular gather
+ *                         and the cover weighting of both supports
+ *                         (layers/hex_patch_geometry.py:82-90,
+ *                          layers/rotating_dot_product.py:9-13), cast to bf16
+ *                         as the input of the tokenizer / Look-bank GEMM.
+ *   svit_embed_post     : after that GEMM, the tokenizer's null softmax and
+ *                         harmonic moments (layers/hex_rotating_harmonic_patch_embed.py:153-242),
+ *                         CLS + position embedding
+ *                         (model/deit_tiny_rot_hex_look.py:305-452), and the
+ *                         Look bank's null softmax (layers/square_patch_dense_grid_look.py:339-355)
+ *                         contracted with the per-slot Look fields into the
+ *                         per-query Look values the attention kernel reads.
+ *   svit_add_layernorm  : residual add + LayerNorm + bf16 cast of the
+ *                         pre-norm transformer block (layers/mini_vit.py:138-170).
+ * Same conventions as intp_b200.h: device pointers, element strides, a CUDA
+ * stream, intp_status return codes; nothing is allocated or freed.
+ */
+#ifndef INTP_SHARE_VIT_H
+#define INTP_SHARE_VIT_H
+
+#include <stdint.h>
+#include "intp_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[b * patches + n, f] = bf16(image[b][pixel_index[n, f]] * weight[f])
+ * image: (batch, image_elems) float32 contiguous; pixel_index: (patches,
+ * features) int32 offsets into one image (already reflected into range);
+ * weight: (features) float32; out: (batch * patches, features) bf16,
+ * row-major.  features % 8 == 0.                                            */
+INTP_API intp_status svit_gather_patches(const float* image, int64_t batch, int64_t image_elems,
+                                         const int32_t* pixel_index, const float* weight, int64_t patches,
+                                         int64_t features, void* out, void* stream);
+
+/* Geometry of the post-GEMM step (one response row per patch).
+ * resp row layout (bf16): [bases x directions tokenizer scores |
+ * for each support s: look_heads x directions Look-bank responses], so Look
+ * pose p = s * directions + d of head h sits at column
+ * bases*directions + s*look_heads*directions + h*directions + d.            */
+typedef struct svit_embed_args {
+  int64_t batch, patches;          /* patches per image (N - 1)                    */
+  int32_t bases, directions;       /* tokenizer: bases x directions, 2*bases = dim */
+  int32_t look_heads, look_poses;  /* look_poses = supports x directions           */
+  int32_t slots;                   /* Look slots per head                          */
+  const void* resp;   int64_t resp_stride;  /* bf16 (batch*patches, >= columns)    */
+  const float* token_null;      /* (bases) null score of each base               */
+  const float* direction_coef;  /* (directions, 2) cos / sin of each direction   */
+  const float* output_bias;     /* (2*bases)                                     */
+  const float* cls;             /* (2*bases) CLS token                           */
+  const float* pos_embed;       /* (patches + 1, 2*bases)                        */
+  const float* look_null;       /* (look_heads) null score of each Look head     */
+  const float* slot_fields;     /* (look_heads, look_poses, slots) Look value of */
+                                /* each slot per pose                            */
+  float* x;                     /* out: (batch, patches + 1, 2*bases) tokens     */
+  float* values;                /* out: (batch, patches, look_heads, slots)      */
+} svit_embed_args;
+
+INTP_API intp_status svit_embed_post(const svit_embed_args* args, void* stream);
+
+/* For r < rows: x[r] += y[r] (when y is not NULL; y bf16), then
+ * h[r] = bf16(LayerNorm(x[r]) * gamma + beta) over `dim` features.
+ * Row r of x / y / h starts at r * x_stride / y_stride / h_stride elements.
+ * dim % 64 == 0 and dim <= 512.                                             */
+INTP_API intp_status svit_add_layernorm(float* x, int64_t x_stride, const void* y, int64_t y_stride,
+                                        const float* gamma, const float* beta, float eps, int64_t rows,
+                                        int64_t dim, void* h, int64_t h_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INTP_SHARE_VIT_H */

@@ -40,6 +40,12 @@ EXPORTED_SYMBOLS = (
     "intp_abi_version",
     "intp_status_string",
 )
+# Every symbol include/intp_share_vit.h declares.
+SHARE_VIT_SYMBOLS = (
+    "svit_gather_patches",
+    "svit_embed_post",
+    "svit_add_layernorm",
+)
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -71,6 +77,21 @@ class SlaForwardArgs(ctypes.Structure):
     ]
 
 
+class SvitEmbedArgs(ctypes.Structure):
+    """Mirror of ``svit_embed_args`` (include/intp_share_vit.h)."""
+
+    _fields_ = [
+        ("batch", _i64), ("patches", _i64),
+        ("bases", _i32), ("directions", _i32),
+        ("look_heads", _i32), ("look_poses", _i32),
+        ("slots", _i32),
+        ("resp", _vp), ("resp_stride", _i64),
+        ("token_null", _vp), ("direction_coef", _vp), ("output_bias", _vp),
+        ("cls", _vp), ("pos_embed", _vp), ("look_null", _vp), ("slot_fields", _vp),
+        ("x", _vp), ("values", _vp),
+    ]
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -90,7 +111,7 @@ def load() -> ctypes.CDLL:
                 f"{LIB_PATH} is not built; run `python -m intp_preliminary_b200.build`"
             )
         lib = ctypes.CDLL(str(LIB_PATH))
-        missing = [name for name in EXPORTED_SYMBOLS if not hasattr(lib, name)]
+        missing = [name for name in EXPORTED_SYMBOLS + SHARE_VIT_SYMBOLS if not hasattr(lib, name)]
         if missing:
             raise NativeLibraryError(f"{LIB_PATH} lacks symbols {missing}")
         lib.sla_forward.argtypes = [ctypes.POINTER(SlaForwardArgs), _vp]
@@ -107,6 +128,12 @@ def load() -> ctypes.CDLL:
         lib.sla_read_status.restype = _i32
         lib.intp_device_info.argtypes = [ctypes.POINTER(_i32)] * 3
         lib.intp_device_info.restype = _i32
+        lib.svit_gather_patches.argtypes = [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp]
+        lib.svit_gather_patches.restype = _i32
+        lib.svit_embed_post.argtypes = [ctypes.POINTER(SvitEmbedArgs), _vp]
+        lib.svit_embed_post.restype = _i32
+        lib.svit_add_layernorm.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, ctypes.c_float, _i64, _i64, _vp, _i64, _vp]
+        lib.svit_add_layernorm.restype = _i32
         lib.intp_abi_version.argtypes = []
         lib.intp_abi_version.restype = _i32
         lib.intp_status_string.argtypes = [_i32]

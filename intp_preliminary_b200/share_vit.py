@@ -48,6 +48,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .look_attention import LookSlots, look_attention_forward
+from .share_vit_ops import add_layernorm, embed_post, gather_patches
 
 IMAGE_SIZE = 224
 IN_CHANS = 3
@@ -231,6 +232,12 @@ def look_slot_basis(unit_xy: torch.Tensor, max_slots: int = 93):
     return table.reshape(n, n).numpy(), basis.permute(1, 2, 0).float().contiguous()  # (P, G, S)
 
 
+def _reflect(index: torch.Tensor, size: int) -> torch.Tensor:
+    """Source index of a reflect-padded coordinate (edge not repeated, like F.pad mode="reflect")."""
+    index = index.abs()
+    return torch.where(index >= size, 2 * (size - 1) - index, index)
+
+
 # ----------------------------------------------------------------------------- modules
 class _RotatingHarmonicTokenizer(nn.Module):
     """Parameters of layers/hex_rotating_harmonic_patch_embed.py (prototype, null, bias)."""
@@ -304,6 +311,19 @@ class ShareViTHalf6d3r(nn.Module):
             self.register_buffer(f"cover_{i}", polar.cover * (reference_mass / polar.cover.sum()), persistent=False)
             self.register_buffer(f"sample_x_{i}", self.supports[i].sample_x, persistent=False)
             self.register_buffer(f"sample_y_{i}", self.supports[i].sample_y, persistent=False)
+        # Fused gather: per patch and feature (support blocks of channel-major
+        # samples, the order of `_patches`), the pixel offset inside one image
+        # after reflect padding, and the cover weight.
+        index_parts, weight_parts = [], []
+        for i, support in enumerate(self.supports):
+            rows = _reflect(support.sample_x - support.pad_x, IMAGE_SIZE)
+            cols = _reflect(support.sample_y - support.pad_y, IMAGE_SIZE)
+            pixel = rows * IMAGE_SIZE + cols
+            for c in range(IN_CHANS):
+                index_parts.append(pixel + c * IMAGE_SIZE * IMAGE_SIZE)
+                weight_parts.append(getattr(self, f"cover_{i}"))
+        self.register_buffer("pixel_index", torch.cat(index_parts, dim=1).to(torch.int32).contiguous(), persistent=False)
+        self.register_buffer("pixel_weight", torch.cat(weight_parts).float().contiguous(), persistent=False)
         theta = torch.arange(DIRECTIONS) * (2 * math.pi / GLOBAL_DIRECTIONS)
         self.register_buffer("direction_coefficients", torch.stack((torch.cos(theta), torch.sin(theta)), -1),
                              persistent=False)
@@ -407,6 +427,90 @@ class ShareViTHalf6d3r(nn.Module):
         pose = torch.cat((look, lnull), -1).softmax(-1)[..., :-1]                 # (B, N, 36, 12)
         return tokens, pose
 
+    def _fused_embed_weights(self, device, dtype=torch.bfloat16):
+        """(W, F): the (576 + 2*216, F0 + F1) bf16 matrix of one GEMM that gives the
+        tokenizer scores summed over both supports and the Look-bank responses of
+        each support, and the per-slot Look fields (36, 12, S) fp32 (cached per
+        weight version)."""
+        key = ("fused", device, dtype, self._weights_key())
+        with self._cache_lock:
+            hit = self._cache.get(key)
+        if hit is not None:
+            return hit
+        mats = self._rendered(device, dtype)
+        tok, look = BASES * DIRECTIONS, LOOK_HEADS * DIRECTIONS
+        f0, f1 = mats[0].shape[1], mats[1].shape[1]
+        w = torch.zeros(tok + 2 * look, f0 + f1, dtype=dtype, device=device)
+        w[:tok, :f0], w[:tok, f0:] = mats[0][:tok], mats[1][:tok]
+        w[tok:tok + look, :f0] = mats[0][tok:]
+        w[tok + look:, f0:] = mats[1][tok:]
+        fields = self.slot_fields().to(device=device, dtype=torch.float32).contiguous()
+        hit = (w, fields)
+        with self._cache_lock:
+            self._cache = {k: v for k, v in self._cache.items() if k[0] != "fused"}
+            self._cache[key] = hit
+        return hit
+
+    @torch.no_grad()
+    def embed_fused(self, image: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """bf16 tokenizer + Look bank on the fused kernels: the residual stream
+        x (B, N+1, 192) fp32 with CLS and position embedding, and the per-slot
+        Look values (B, N, 36, S) fp32.  Same math as ``embed`` + ``look_values``."""
+        if image.ndim != 4 or tuple(image.shape[1:]) != (IN_CHANS, IMAGE_SIZE, IMAGE_SIZE):
+            raise ValueError(f"expected images (B, {IN_CHANS}, {IMAGE_SIZE}, {IMAGE_SIZE})")
+        batch, n = image.shape[0], self.num_patches
+        image = image.float().contiguous()
+        w, fields = self._fused_embed_weights(image.device)
+        patches = gather_patches(image, self.pixel_index, self.pixel_weight)
+        resp = patches @ w.t()
+        x = torch.empty(batch, n + 1, EMBED_DIM, dtype=torch.float32, device=image.device)
+        values = torch.empty(batch, n, LOOK_HEADS, fields.shape[-1], dtype=torch.float32, device=image.device)
+        embed_post(resp, batch=batch, patches=n, bases=BASES, directions=DIRECTIONS, look_heads=LOOK_HEADS,
+                   look_poses=2 * DIRECTIONS, token_null=self.patch_embed.null_score.detach().float().contiguous(),
+                   direction_coef=self.direction_coefficients.contiguous(),
+                   output_bias=self.patch_embed.output_bias.detach().float().contiguous(),
+                   cls=self.cls_token.detach().float().reshape(-1).contiguous(),
+                   pos_embed=self.pos_embed.detach().float().reshape(n + 1, EMBED_DIM).contiguous(),
+                   look_null=self.look_bank.null_score.detach().float().contiguous(), slot_fields=fields,
+                   x=x, values=values)
+        return x, values
+
+    @torch.no_grad()
+    def trunk_fused(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool = False) -> torch.Tensor:
+        """The 12 blocks and the final LayerNorm in bf16 on the fused kernels:
+        add + LayerNorm + cast in one pass, cuBLAS linears (bias in the epilogue),
+        Look attention writing token-major output.  ``x`` is updated in place.
+        Returns the normalised tokens (B, N+1, 192) bf16, or only the CLS rows
+        (B, 192) when ``cls_only``."""
+        batch, n1 = x.shape[0], x.shape[1]
+        rows = batch * n1
+        head_dim = EMBED_DIM // HEADS
+        weights = self._trunk_weights(torch.bfloat16)
+        scale = 1.0 / math.sqrt(head_dim)
+        events = self.attention_events
+        attn = torch.empty(batch, n1, HEADS, head_dim, dtype=torch.bfloat16, device=x.device)
+        attn_bhnd = attn.permute(0, 2, 1, 3)
+        y = None
+        for layer, blk in enumerate(self.blocks):
+            w_qkv, b_qkv, w_proj, b_proj, w_fc1, b_fc1, w_fc2, b_fc2 = weights[layer]
+            h = add_layernorm(x, y, blk.norm1.weight, blk.norm1.bias, 1e-6)
+            qkv = F.linear(h, w_qkv, b_qkv).view(batch, n1, 3, HEADS, head_dim)
+            q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+            pose_l = values[:, :, HEADS * layer:HEADS * (layer + 1)]
+            if events is not None:
+                start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+            look_attention_forward(q, k, v, pose_l, self.look_slots, scale=scale, out=attn_bhnd)
+            if events is not None:
+                stop.record()
+                events.append((start, stop))
+            y = F.linear(attn.view(rows, EMBED_DIM), w_proj, b_proj)
+            h = add_layernorm(x, y, blk.norm2.weight, blk.norm2.bias, 1e-6)
+            y = F.linear(F.gelu(F.linear(h, w_fc1, b_fc1)), w_fc2, b_fc2)
+        if cls_only:
+            return add_layernorm(x[:, 0], y.view(batch, n1, EMBED_DIM)[:, 0], self.norm.weight, self.norm.bias, 1e-6)
+        return add_layernorm(x, y, self.norm.weight, self.norm.bias, 1e-6).view(batch, n1, EMBED_DIM)
+
     def slot_fields(self) -> torch.Tensor:
         """F[h, p, s] = sum_g basis[p, g, s] * grid[h, g]: the Look field value of
         slot s for head h and pose p, (36, 12, S) fp32."""
@@ -461,6 +565,10 @@ class ShareViTHalf6d3r(nn.Module):
 
     @torch.no_grad()
     def forward_features(self, image: torch.Tensor) -> torch.Tensor:
+        """Normalised tokens (B, N+1, 192) fp32."""
+        if self.precision == "bf16":
+            x, values = self.embed_fused(image)
+            return self.trunk_fused(x, values).float()
         tokens, pose = self.embed(image)
         values = self.look_values(pose)
         scale = 1.0 / math.sqrt(EMBED_DIM // HEADS)
@@ -481,4 +589,8 @@ class ShareViTHalf6d3r(nn.Module):
 
     @torch.no_grad()
     def forward(self, image: torch.Tensor) -> torch.Tensor:
+        if self.precision == "bf16":
+            x, values = self.embed_fused(image)
+            cls = self.trunk_fused(x, values, cls_only=True)
+            return F.linear(cls.float(), self.head.weight, self.head.bias)
         return F.linear(self.forward_features(image)[:, 0], self.head.weight, self.head.bias)

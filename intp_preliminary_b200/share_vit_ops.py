@@ -1,0 +1,115 @@
+"""Python side of the fused SHARE-ViT steps around the Look attention
+(C ABI in include/intp_share_vit.h, kernels in csrc/share_vit_ops.cu).
+
+Each function validates its tensors, then launches one kernel of
+``libintp_b200.so`` on the current stream.  There is no PyTorch fallback:
+CPU tensors, wrong dtypes or layouts raise ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None else None)
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require(cond: bool, message: str) -> None:
+    if not cond:
+        raise ValueError(message)
+
+
+def gather_patches(image: torch.Tensor, pixel_index: torch.Tensor, weight: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[b*N + n, f] = bf16(image[b].flatten()[pixel_index[n, f]] * weight[f])``.
+
+    image (B, C, H, W) float32 contiguous CUDA; pixel_index (N, F) int32;
+    weight (F,) float32.  Returns (B*N, F) bf16."""
+    _require(image.is_cuda and image.dtype == torch.float32 and image.is_contiguous(),
+             "image must be a contiguous float32 CUDA tensor")
+    _require(pixel_index.dtype == torch.int32 and pixel_index.ndim == 2 and pixel_index.is_contiguous(),
+             "pixel_index must be a contiguous (N, F) int32 tensor")
+    _require(weight.dtype == torch.float32 and weight.ndim == 1 and weight.shape[0] == pixel_index.shape[1],
+             "weight must be a float32 (F,) tensor")
+    _require(pixel_index.device == image.device and weight.device == image.device, "tensors must share a device")
+    batch = image.shape[0]
+    patches, features = pixel_index.shape
+    if out is None:
+        out = torch.empty((batch * patches, features), dtype=torch.bfloat16, device=image.device)
+    _require(out.shape == (batch * patches, features) and out.dtype == torch.bfloat16 and out.is_contiguous(),
+             "out must be a contiguous (B*N, F) bf16 tensor")
+    status = _lib.load().svit_gather_patches(
+        _ptr(image), batch, image[0].numel() if batch else 0, _ptr(pixel_index), _ptr(weight), patches, features,
+        _ptr(out), _stream(image.device))
+    _lib.check(status, "hex patch gather")
+    return out
+
+
+def embed_post(resp: torch.Tensor, *, batch: int, patches: int, bases: int, directions: int, look_heads: int,
+               look_poses: int, token_null: torch.Tensor, direction_coef: torch.Tensor, output_bias: torch.Tensor,
+               cls: torch.Tensor, pos_embed: torch.Tensor, look_null: torch.Tensor, slot_fields: torch.Tensor,
+               x: torch.Tensor, values: torch.Tensor) -> None:
+    """Tokens (with CLS and position embedding) into ``x`` (B, N+1, 2*bases) and
+    per-slot Look values into ``values`` (B, N, look_heads, slots), from the
+    bf16 response rows ``resp`` (B*N, >= bases*directions + look_poses*look_heads)."""
+    dev = resp.device
+    _require(resp.is_cuda and resp.dtype == torch.bfloat16 and resp.ndim == 2 and resp.stride(1) == 1,
+             "resp must be a bf16 CUDA matrix with unit column stride")
+    _require(resp.shape[0] == batch * patches, "resp must have batch * patches rows")
+    fp32 = (token_null, direction_coef, output_bias, cls, pos_embed, look_null, slot_fields, x, values)
+    for t in fp32:
+        _require(t.device == dev and t.dtype == torch.float32 and t.is_contiguous(),
+                 "parameters and outputs must be contiguous float32 tensors on resp's device")
+    slots = slot_fields.shape[-1]
+    _require(slot_fields.shape == (look_heads, look_poses, slots), "slot_fields must be (look_heads, look_poses, S)")
+    _require(x.shape == (batch, patches + 1, 2 * bases), "x must be (B, N+1, 2*bases)")
+    _require(values.shape == (batch, patches, look_heads, slots), "values must be (B, N, look_heads, S)")
+    a = _lib.SvitEmbedArgs()
+    a.batch, a.patches = batch, patches
+    a.bases, a.directions, a.look_heads, a.look_poses, a.slots = bases, directions, look_heads, look_poses, slots
+    a.resp, a.resp_stride = resp.data_ptr(), resp.stride(0)
+    a.token_null, a.direction_coef, a.output_bias = token_null.data_ptr(), direction_coef.data_ptr(), output_bias.data_ptr()
+    a.cls, a.pos_embed, a.look_null, a.slot_fields = cls.data_ptr(), pos_embed.data_ptr(), look_null.data_ptr(), slot_fields.data_ptr()
+    a.x, a.values = x.data_ptr(), values.data_ptr()
+    status = _lib.load().svit_embed_post(ctypes.byref(a), _stream(dev))
+    _lib.check(status, "tokenizer / Look-bank post-processing")
+
+
+def add_layernorm(x: torch.Tensor, y: torch.Tensor | None, weight: torch.Tensor, bias: torch.Tensor, eps: float,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x += y`` (when given, in place) then ``out = bf16(LayerNorm(x))`` over the last dim.
+
+    x float32 (..., dim) with unit last stride and rows at a common stride;
+    y bf16 of the same row shape or None."""
+    dim = x.shape[-1]
+    _require(x.is_cuda and x.dtype == torch.float32 and x.stride(-1) == 1, "x must be float32 CUDA, unit last stride")
+    xr = x.reshape(-1, dim)
+    _require(xr.data_ptr() == x.data_ptr(), "x rows must be addressable with one stride")
+    rows = xr.shape[0]
+    if y is not None:
+        _require(y.dtype == torch.bfloat16 and y.device == x.device and y.shape[-1] == dim, "y must be bf16 like x")
+        yr = y.reshape(-1, dim)
+        _require(yr.shape[0] == rows and yr.stride(-1) == 1, "y must match x's rows")
+    else:
+        yr = None
+    for t in (weight, bias):
+        _require(t.dtype == torch.float32 and t.is_contiguous() and t.shape == (dim,) and t.device == x.device,
+                 "LayerNorm weight and bias must be contiguous float32 (dim,)")
+    if out is None:
+        out = torch.empty((rows, dim), dtype=torch.bfloat16, device=x.device)
+    outr = out.reshape(-1, dim)
+    _require(out.dtype == torch.bfloat16 and outr.shape[0] == rows and outr.stride(-1) == 1, "out must be bf16 rows")
+    status = _lib.load().svit_add_layernorm(
+        _ptr(xr), xr.stride(0), _ptr(yr), yr.stride(0) if yr is not None else 0, _ptr(weight), _ptr(bias),
+        float(eps), rows, dim, _ptr(outr), outr.stride(0), _stream(x.device))
+    _lib.check(status, "add + LayerNorm")
+    return out

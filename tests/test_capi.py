@@ -12,20 +12,44 @@ from intp_preliminary_b200 import _lib
 from intp_preliminary_b200.look_attention import LookSlots
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "intp_b200.h"
+SVIT_HEADER = HEADER.with_name("intp_share_vit.h")
 
 
-def _declared_functions():
-    text = HEADER.read_text()
+def _declared_functions(header=HEADER):
+    text = header.read_text()
     return sorted(set(re.findall(r"INTP_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)))
 
 
 def test_library_exports_every_header_symbol():
     lib = _lib.load()
-    declared = _declared_functions()
-    assert declared, "no declarations found"
-    assert set(declared) == set(_lib.EXPORTED_SYMBOLS)
-    for name in declared:
-        assert hasattr(lib, name), name
+    for header, expected in ((HEADER, _lib.EXPORTED_SYMBOLS), (SVIT_HEADER, _lib.SHARE_VIT_SYMBOLS)):
+        declared = _declared_functions(header)
+        assert declared, f"no declarations found in {header.name}"
+        assert set(declared) == set(expected)
+        for name in declared:
+            assert hasattr(lib, name), name
+    headers = sorted(p.name for p in HEADER.parent.glob("*.h"))
+    assert headers == ["intp_b200.h", "intp_share_vit.h"]
+
+
+def test_svit_struct_layout_matches_header_field_order():
+    text = SVIT_HEADER.read_text()
+    body = text[text.index("typedef struct svit_embed_args"):text.index("} svit_embed_args;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = re.findall(r"(\w+)\s*[;,]", body)
+    assert names == [f[0] for f in _lib.SvitEmbedArgs._fields_]
+
+
+def test_svit_host_side_argument_checks():
+    lib = _lib.load()
+    # zero-sized work is a no-op; bad sizes are rejected before any launch
+    assert lib.svit_gather_patches(None, 0, 0, None, None, 0, 0, None, None) == _lib.INTP_OK
+    assert lib.svit_gather_patches(None, -1, 0, None, None, 1, 8, None, None) == _lib.INTP_ERR_ARGUMENT
+    assert lib.svit_add_layernorm(None, 0, None, 0, None, None, 1e-6, 0, 192, None, 0, None) == _lib.INTP_OK
+    assert lib.svit_add_layernorm(None, 0, None, 0, None, None, 1e-6, 3, 192, None, 0, None) == _lib.INTP_ERR_ARGUMENT
+    a = _lib.SvitEmbedArgs()
+    a.batch, a.patches, a.bases, a.directions, a.look_heads, a.look_poses, a.slots = 1, 4, 96, 6, 36, 12, 200
+    assert lib.svit_embed_post(ctypes.byref(a), None) == _lib.INTP_ERR_SHAPE
 
 
 def test_abi_version_and_status_strings():

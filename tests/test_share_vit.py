@@ -66,3 +66,37 @@ def test_cpu_port_matches_reference_logits(model):
 
     images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(int(GOLD["image_seed"])))
     np.testing.assert_allclose(reference_forward_cpu(model, images).numpy(), GOLD["logits"], atol=1e-4, rtol=1e-4)
+
+
+def test_fused_gather_tables_reproduce_reflect_gather(model):
+    """pixel_index / pixel_weight (read by the fused gather kernel) give exactly
+    the reflect-padded, cover-weighted patches of both supports."""
+    images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(5))
+    ref = torch.cat([model._patches(images, 0), model._patches(images, 1)], dim=-1)
+    got = images.flatten(1)[:, model.pixel_index.long()] * model.pixel_weight
+    assert model.pixel_index.shape == (195, 3 * (448 + 112))
+    assert int(model.pixel_index.min()) >= 0 and int(model.pixel_index.max()) < 3 * 224 * 224
+    torch.testing.assert_close(got, ref, rtol=0, atol=0)
+
+
+def test_fused_embed_weight_matrix_layout(model):
+    """One GEMM against the fused matrix gives the tokenizer scores summed over
+    both supports and the Look-bank responses of each support."""
+    images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(6))
+    p0, p1 = model._patches(images, 0).reshape(-1, 1344), model._patches(images, 1).reshape(-1, 336)
+    w, fields = model._fused_embed_weights(torch.device("cpu"), torch.float32)
+    mats = model._rendered(torch.device("cpu"), torch.float32)
+    resp = torch.cat([p0, p1], dim=1) @ w.t()
+    r0, r1 = p0 @ mats[0].t(), p1 @ mats[1].t()
+    torch.testing.assert_close(resp[:, :576], r0[:, :576] + r1[:, :576], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(resp[:, 576:792], r0[:, 576:], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(resp[:, 792:], r1[:, 576:], rtol=1e-4, atol=1e-4)
+    assert fields.shape == (36, 12, 68)
+
+
+def test_fused_op_wrappers_reject_cpu_tensors():
+    from intp_preliminary_b200 import share_vit_ops as ops
+    with pytest.raises(ValueError):
+        ops.gather_patches(torch.zeros(1, 3, 8, 8), torch.zeros(2, 8, dtype=torch.int32), torch.zeros(8))
+    with pytest.raises(ValueError):
+        ops.add_layernorm(torch.zeros(4, 192), None, torch.ones(192), torch.zeros(192), 1e-6)

@@ -47,3 +47,25 @@ def test_bf16_batch_forward_is_finite_and_batch_consistent(cuda_device):
     part = model(images[:16])
     assert torch.isfinite(full).all()
     assert (full[:16] - part).abs().max().item() <= 1e-2
+
+
+def test_graphed_and_pipelined_forward_match_eager(cuda_device):
+    from intp_preliminary_b200.serving import GraphedForward, PipelinedInference
+
+    model = _model("bf16", cuda_device)
+    g = torch.Generator().manual_seed(17)
+    host = [torch.randn(8, 3, 224, 224, generator=g).pin_memory() for _ in range(3)]
+    eager = [model(h.to(cuda_device)).float().cpu() for h in host]
+
+    buf = host[1].to(cuda_device)
+    graphed = GraphedForward(model, buf)
+    buf.copy_(host[2].to(cuda_device))
+    torch.testing.assert_close(graphed.replay().float().cpu(), eager[2], rtol=0, atol=0)
+
+    pipe = PipelinedInference(model, 8, cuda_device)
+    outs = [torch.empty(8, 100).pin_memory() for _ in range(5)]
+    pipe.run([host[i % 3] for i in range(5)], outs)
+    torch.cuda.synchronize(cuda_device)
+    for i in range(5):
+        torch.testing.assert_close(outs[i], eager[i % 3], rtol=0, atol=0)
+    check_device_status(cuda_device)

@@ -1,0 +1,85 @@
+"""Fused SHARE-ViT kernels (gather, post-GEMM, add + LayerNorm) against the
+plain PyTorch formulation of the same steps."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from intp_preliminary_b200 import share_vit_ops as ops
+from intp_preliminary_b200.share_vit import EMBED_DIM, ShareViTHalf6d3r
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model(cuda_device):
+    return ShareViTHalf6d3r(precision="bf16").init_weights(seed=1, look_grid_std=0.5).to(cuda_device)
+
+
+def test_gather_patches_matches_reflect_gather(model, cuda_device):
+    images = torch.randn(3, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(2))
+    got = ops.gather_patches(images, model.pixel_index, model.pixel_weight)
+    ref = torch.cat([model._patches(images, 0), model._patches(images, 1)], dim=-1).reshape(3 * 195, -1)
+    assert torch.equal(got, ref.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("rows,dim", [(1, 192), (37, 192), (50432 // 16, 192), (9, 64), (5, 512)])
+def test_add_layernorm_matches_torch(cuda_device, rows, dim):
+    g = torch.Generator(cuda_device).manual_seed(rows)
+    x = torch.randn(rows, dim, device=cuda_device, generator=g) * 3 + 1
+    y = torch.randn(rows, dim, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = torch.randn(dim, device=cuda_device, generator=g)
+    b = torch.randn(dim, device=cuda_device, generator=g)
+    x_ref = x + y.float()
+    h_ref = F.layer_norm(x_ref, (dim,), w, b, 1e-6)
+    h = ops.add_layernorm(x, y, w, b, 1e-6)
+    assert torch.equal(x, x_ref)
+    torch.testing.assert_close(h.float(), h_ref, atol=3e-2, rtol=1e-2)
+    assert (h.float() - h_ref.to(torch.bfloat16).float()).abs().max() <= 2 * 2 ** -8 * h_ref.abs().max()
+    h2 = ops.add_layernorm(x, None, w, b, 1e-6)
+    torch.testing.assert_close(h2.float(), h_ref, atol=3e-2, rtol=1e-2)
+
+
+def test_add_layernorm_on_strided_rows(cuda_device):
+    x = torch.randn(4, 7, 192, device=cuda_device)
+    y = torch.randn(4, 7, 192, device=cuda_device).to(torch.bfloat16)
+    w, b = torch.ones(192, device=cuda_device), torch.zeros(192, device=cuda_device)
+    x0 = x.clone()
+    h = ops.add_layernorm(x[:, 0], y[:, 0], w, b, 1e-6)
+    ref = F.layer_norm(x0[:, 0] + y[:, 0].float(), (192,), w, b, 1e-6)
+    torch.testing.assert_close(h.float(), ref, atol=3e-2, rtol=1e-2)
+    assert torch.equal(x[:, 1:], x0[:, 1:])
+
+
+def test_embed_fused_matches_unfused(model, cuda_device):
+    images = torch.randn(4, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(3))
+    x, values = model.embed_fused(images)
+    tokens, pose = model.embed(images)
+    ref_values = model.look_values(pose)
+    ref_x = torch.cat((model.cls_token.expand(4, -1, -1), tokens), dim=1) + model.pos_embed
+    torch.testing.assert_close(x, ref_x, atol=3e-2, rtol=3e-2)
+    torch.testing.assert_close(values, ref_values, atol=3e-2, rtol=3e-2)
+    assert torch.equal(x[:, 0], (model.cls_token[0, 0] + model.pos_embed[0, 0]).expand(4, -1))
+
+
+def test_fused_forward_matches_unfused_bf16(model, cuda_device):
+    images = torch.randn(6, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(4))
+    fused = model(images)
+    tokens, pose = model.embed(images)
+    values = model.look_values(pose)
+    scale = 1.0 / math.sqrt(64)
+    from intp_preliminary_b200.look_attention import look_attention_forward
+
+    def attend(layer, q, k, v, out):
+        return look_attention_forward(q, k, v, values[:, :, 3 * layer:3 * layer + 3], model.look_slots, scale=scale,
+                                      out=out)[0]
+
+    feats = model.trunk(tokens, attend)
+    ref = F.linear(feats[:, 0], model.head.weight, model.head.bias)
+    err = (fused - ref).abs().max().item()
+    assert err <= 0.05 * ref.abs().max().item(), err
+    assert fused.shape == (6, 100) and torch.isfinite(fused).all()
+    feats_fused = model.forward_features(images)
+    assert feats_fused.shape == (6, 196, EMBED_DIM)
