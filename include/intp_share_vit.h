@@ -60,7 +60,9 @@ typedef struct svit_embed_args {
   const float* slot_fields;     /* (look_heads, look_poses, slots) Look value of */
                                 /* each slot per pose                            */
   float* x;                     /* out: (batch, patches + 1, 2*bases) tokens     */
-  float* values;                /* out: (batch, patches, look_heads, slots)      */
+  float* values;                /* out: (batch, look_heads, patches, slots):     */
+                                /* per image and head, the patches' slot values  */
+                                /* are contiguous                                */
 } svit_embed_args;
 
 INTP_API intp_status svit_embed_post(const svit_embed_args* args, void* stream);

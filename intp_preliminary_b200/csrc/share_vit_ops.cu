@@ -50,7 +50,7 @@ __device__ __forceinline__ float bf16_at(const __nv_bfloat16* p, int64_t i) { re
 
 // Phase 1: one warp per patch - tokenizer moments straight into x, the Look
 // pose (null softmax per head) into shared memory.  Phase 2: for each head,
-// values[row, h, s] = sum_p pose[row, h, p] * fields[h, p, s] with the head's
+// values[b, h, n, s] = sum_p pose[row, h, p] * fields[h, p, s] with the head's
 // fields in shared memory and each thread keeping one slot's column in
 // registers while it walks the CTA's patches.
 template <int D, int LP>
@@ -141,11 +141,18 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
       for (int t = tg; t < kPostTokens; t += G) {
         const int64_t row = row0 + t;
         if (row >= rows) break;
-        const float* pose = pose_s + (t * LH + h) * LP;
+        const int64_t b = row / a.patches, n = row - b * a.patches;
+        const float4* pose = reinterpret_cast<const float4*>(pose_s + (t * LH + h) * LP);
         float v = 0.f;
 #pragma unroll
-        for (int pp = 0; pp < LP; ++pp) v = fmaf(pose[pp], f[pp], v);
-        a.values[(row * LH + h) * S + s] = v;
+        for (int q = 0; q < LP / 4; ++q) {
+          const float4 p4 = pose[q];
+          v = fmaf(p4.x, f[4 * q], v);
+          v = fmaf(p4.y, f[4 * q + 1], v);
+          v = fmaf(p4.z, f[4 * q + 2], v);
+          v = fmaf(p4.w, f[4 * q + 3], v);
+        }
+        a.values[((b * LH + h) * a.patches + n) * S + s] = v;
       }
     }
   }
@@ -240,6 +247,7 @@ extern "C" INTP_API intp_status svit_embed_post(const svit_embed_args* a, void* 
     return INTP_ERR_SHAPE;
   // The half6d3r geometry: 6 directions, 2 supports x 6 directions of Look pose.
   if (a->directions != 6 || a->look_poses != 12) return INTP_ERR_UNSUPPORTED;
+  static_assert((12 % 4) == 0, "pose rows are read as float4");
   constexpr int D = 6, LP = 12;
   const int64_t columns = static_cast<int64_t>(a->bases) * D + static_cast<int64_t>(LP) * a->look_heads;
   if (a->resp_stride < columns) return INTP_ERR_SHAPE;

@@ -455,7 +455,8 @@ class ShareViTHalf6d3r(nn.Module):
     def embed_fused(self, image: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """bf16 tokenizer + Look bank on the fused kernels: the residual stream
         x (B, N+1, 192) fp32 with CLS and position embedding, and the per-slot
-        Look values (B, N, 36, S) fp32.  Same math as ``embed`` + ``look_values``."""
+        Look values (B, N, 36, S) fp32 - a view of a (B, 36, N, S) buffer, so
+        each head's rows are contiguous.  Same math as ``embed`` + ``look_values``."""
         if image.ndim != 4 or tuple(image.shape[1:]) != (IN_CHANS, IMAGE_SIZE, IMAGE_SIZE):
             raise ValueError(f"expected images (B, {IN_CHANS}, {IMAGE_SIZE}, {IMAGE_SIZE})")
         batch, n = image.shape[0], self.num_patches
@@ -464,7 +465,7 @@ class ShareViTHalf6d3r(nn.Module):
         patches = gather_patches(image, self.pixel_index, self.pixel_weight)
         resp = patches @ w.t()
         x = torch.empty(batch, n + 1, EMBED_DIM, dtype=torch.float32, device=image.device)
-        values = torch.empty(batch, n, LOOK_HEADS, fields.shape[-1], dtype=torch.float32, device=image.device)
+        values = torch.empty(batch, LOOK_HEADS, n, fields.shape[-1], dtype=torch.float32, device=image.device)
         embed_post(resp, batch=batch, patches=n, bases=BASES, directions=DIRECTIONS, look_heads=LOOK_HEADS,
                    look_poses=2 * DIRECTIONS, token_null=self.patch_embed.null_score.detach().float().contiguous(),
                    direction_coef=self.direction_coefficients.contiguous(),
@@ -473,7 +474,7 @@ class ShareViTHalf6d3r(nn.Module):
                    pos_embed=self.pos_embed.detach().float().reshape(n + 1, EMBED_DIM).contiguous(),
                    look_null=self.look_bank.null_score.detach().float().contiguous(), slot_fields=fields,
                    x=x, values=values)
-        return x, values
+        return x, values.permute(0, 2, 1, 3)
 
     @torch.no_grad()
     def trunk_fused(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool = False) -> torch.Tensor:

@@ -59,7 +59,7 @@ def embed_post(resp: torch.Tensor, *, batch: int, patches: int, bases: int, dire
                cls: torch.Tensor, pos_embed: torch.Tensor, look_null: torch.Tensor, slot_fields: torch.Tensor,
                x: torch.Tensor, values: torch.Tensor) -> None:
     """Tokens (with CLS and position embedding) into ``x`` (B, N+1, 2*bases) and
-    per-slot Look values into ``values`` (B, N, look_heads, slots), from the
+    per-slot Look values into ``values`` (B, look_heads, N, slots), from the
     bf16 response rows ``resp`` (B*N, >= bases*directions + look_poses*look_heads)."""
     dev = resp.device
     _require(resp.is_cuda and resp.dtype == torch.bfloat16 and resp.ndim == 2 and resp.stride(1) == 1,
@@ -72,7 +72,7 @@ def embed_post(resp: torch.Tensor, *, batch: int, patches: int, bases: int, dire
     slots = slot_fields.shape[-1]
     _require(slot_fields.shape == (look_heads, look_poses, slots), "slot_fields must be (look_heads, look_poses, S)")
     _require(x.shape == (batch, patches + 1, 2 * bases), "x must be (B, N+1, 2*bases)")
-    _require(values.shape == (batch, patches, look_heads, slots), "values must be (B, N, look_heads, S)")
+    _require(values.shape == (batch, look_heads, patches, slots), "values must be (B, look_heads, N, S)")
     a = _lib.SvitEmbedArgs()
     a.batch, a.patches = batch, patches
     a.bases, a.directions, a.look_heads, a.look_poses, a.slots = bases, directions, look_heads, look_poses, slots
