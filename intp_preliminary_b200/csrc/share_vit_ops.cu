@@ -57,8 +57,7 @@ template <int D, int LP>
 __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_embed_args a) {
   extern __shared__ __align__(16) float smem_post[];
   const int LH = a.look_heads, S = a.slots;
-  float* pose_s = smem_post;                          // [kPostTokens][LH][LP]
-  float* field_s = smem_post + kPostTokens * LH * LP;  // [2][LP][S]
+  float* pose_s = smem_post;  // [kPostTokens][LH][LP]
   const int64_t rows = a.batch * a.patches;
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kPostTokens;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,10 +81,10 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
         sc[d] = bf16_at(r, p * D + d);
         mx = fmaxf(mx, sc[d]);
       }
-      float sum = expf(null - mx), tx = 0.f, ty = 0.f;
+      float sum = __expf(null - mx), tx = 0.f, ty = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) {
-        const float e = expf(sc[d] - mx);
+        const float e = __expf(sc[d] - mx);
         sum += e;
         tx = fmaf(e, a.direction_coef[2 * d], tx);
         ty = fmaf(e, a.direction_coef[2 * d + 1], ty);
@@ -109,10 +108,10 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
         sc[pp] = bf16_at(r, look0 + static_cast<int64_t>(pp / D) * LH * D + h * D + pp % D);
         mx = fmaxf(mx, sc[pp]);
       }
-      float sum = expf(null - mx);
+      float sum = __expf(null - mx);
 #pragma unroll
       for (int pp = 0; pp < LP; ++pp) {
-        sc[pp] = expf(sc[pp] - mx);
+        sc[pp] = __expf(sc[pp] - mx);
         sum += sc[pp];
       }
       const float inv = 1.f / sum;
@@ -122,38 +121,47 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
     }
   }
 
-  // Phase 2.  Thread -> (slot s, token group tg): tokens tg, tg + G, ...
-  const int G = kPostThreads / S;                // token groups (>= 2 for S <= 128)
-  const int s = threadIdx.x % S, tg = threadIdx.x / S;
-  auto load_fields = [&](int h, float* dst) {
-    const float* src = a.slot_fields + static_cast<int64_t>(h) * LP * S;
-    for (int i = threadIdx.x; i < LP * S; i += kPostThreads) dst[i] = __ldg(src + i);
-  };
-  load_fields(0, field_s);
-  for (int h = 0; h < LH; ++h) {
-    __syncthreads();  // pose_s complete (h == 0); fields of h staged; previous buffer free
-    if (h + 1 < LH) load_fields(h + 1, field_s + ((h + 1) & 1) * LP * S);
-    if (tg < G) {
-      const float* fs = field_s + (h & 1) * LP * S;
-      float f[LP];
+  // Phase 2.  Thread -> (head, quad of 4 slots): the quad's 4 x LP fields stay
+  // in registers while the thread walks the CTA's patches (48 FMAs per three
+  // 16-byte shared loads and one 16-byte store); heads go round by round.
+  // out_base[t]: offset of patch t's (head 0, slot 0) value; head h adds h * patches * S.
+  __shared__ int64_t out_base[kPostTokens];
+  if (threadIdx.x < kPostTokens) {
+    const int64_t row = row0 + threadIdx.x;
+    const int64_t b = row / a.patches, n = row - b * a.patches;
+    out_base[threadIdx.x] = row < rows ? (b * LH * a.patches + n) * S : -1;
+  }
+  __syncthreads();
+  const int quads = S / 4;
+  const int heads_per_round = kPostThreads / quads;
+  const int64_t head_step = a.patches * S;
+  for (int h0 = 0; h0 < LH; h0 += heads_per_round) {
+    const int h = h0 + static_cast<int>(threadIdx.x) / quads, q = static_cast<int>(threadIdx.x) % quads;
+    if (h >= LH || threadIdx.x >= heads_per_round * quads) continue;
+    float4 f[LP];
+    const float4* src = reinterpret_cast<const float4*>(a.slot_fields + static_cast<int64_t>(h) * LP * S) + q;
 #pragma unroll
-      for (int pp = 0; pp < LP; ++pp) f[pp] = fs[pp * S + s];
-      for (int t = tg; t < kPostTokens; t += G) {
-        const int64_t row = row0 + t;
-        if (row >= rows) break;
-        const int64_t b = row / a.patches, n = row - b * a.patches;
-        const float4* pose = reinterpret_cast<const float4*>(pose_s + (t * LH + h) * LP);
-        float v = 0.f;
+    for (int pp = 0; pp < LP; ++pp) f[pp] = __ldg(src + pp * quads);
+    const int64_t head_off = h * head_step + 4 * q;
+    for (int t = 0; t < kPostTokens; ++t) {
+      const int64_t base = out_base[t];
+      if (base < 0) break;
+      const float4* pose = reinterpret_cast<const float4*>(pose_s + (t * LH + h) * LP);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int q = 0; q < LP / 4; ++q) {
-          const float4 p4 = pose[q];
-          v = fmaf(p4.x, f[4 * q], v);
-          v = fmaf(p4.y, f[4 * q + 1], v);
-          v = fmaf(p4.z, f[4 * q + 2], v);
-          v = fmaf(p4.w, f[4 * q + 3], v);
+      for (int c = 0; c < LP / 4; ++c) {
+        const float4 p4 = pose[c];
+        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 fe = f[4 * c + e];
+          v.x = fmaf(pv[e], fe.x, v.x);
+          v.y = fmaf(pv[e], fe.y, v.y);
+          v.z = fmaf(pv[e], fe.z, v.z);
+          v.w = fmaf(pv[e], fe.w, v.w);
         }
-        a.values[((b * LH + h) * a.patches + n) * S + s] = v;
       }
+      *reinterpret_cast<float4*>(a.values + base + head_off) = v;
     }
   }
 }
@@ -255,7 +263,8 @@ extern "C" INTP_API intp_status svit_embed_post(const svit_embed_args* a, void* 
       !a->look_null || !a->slot_fields || !a->x || !a->values)
     return INTP_ERR_ARGUMENT;
   if (!aligned(a->x, 8)) return INTP_ERR_LAYOUT;
-  const size_t smem = (static_cast<size_t>(kPostTokens) * a->look_heads * LP + 2 * LP * a->slots) * sizeof(float);
+  if (a->slots % 4 || !aligned(a->slot_fields, 16) || !aligned(a->values, 16)) return INTP_ERR_LAYOUT;
+  const size_t smem = static_cast<size_t>(kPostTokens) * a->look_heads * LP * sizeof(float);
   if (smem > 200 * 1024) return INTP_ERR_SHAPE;
   auto kernel = embed_post_kernel<D, LP>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
