@@ -100,6 +100,34 @@ typedef struct sla_forward_args {
  * reported through *args->status (read it with sla_read_status).            */
 INTP_API intp_status sla_forward(const sla_forward_args* args, void* stream);
 
+/* Arguments of the structured-Look-attention backward.  `fwd` repeats the
+ * forward call (fwd.out = the forward output O, fwd.lse = its LSE, required),
+ * grad_out is dL/dO with the layout rules of q.  Results are float32,
+ * contiguous, and each may be NULL when not wanted:
+ *   grad_q, grad_k, grad_v : (B, H, N, D)
+ *   grad_pose              : (B, Np, H, P)   (FIELDS and SLOTS modes; in SLOTS
+ *                            mode P = number of slots: dL/d per-slot value)
+ *   grad_fields            : (H, P, Np, Np)  (FIELDS mode; zero-filled by the
+ *                            caller, accumulated with atomics over the batch)
+ *   grad_dense             : (B, H, Np, Np)  (when fwd.dense is set)
+ * delta: (B, H, N) float32 scratch.                                          */
+typedef struct sla_backward_args {
+  sla_forward_args fwd;
+  const void* grad_out; int64_t grad_out_stride[4];
+  float* grad_q; float* grad_k; float* grad_v;
+  float* grad_pose;
+  float* grad_fields;
+  float* grad_dense;
+  float* delta;
+} sla_backward_args;
+
+/* Structured Look attention backward.  Replaces the launch of
+ * `_structured_look_probability_score_grad` and the batched matmuls that follow
+ * it in `_StructuredLookAttention.backward`
+ * (layers/triton_structured_look_attention.py:172-292, 341-409); flash-style:
+ * P is recomputed from the LSE, no N x N buffer is needed beyond grad_dense. */
+INTP_API intp_status sla_backward(const sla_backward_args* args, void* stream);
+
 /* Bytes needed by the packed slot table and the tile flags for sequence N. */
 INTP_API intp_status sla_slot_table_bytes(int64_t seq, int64_t* packed_bytes, int64_t* flag_bytes);
 
@@ -119,6 +147,14 @@ INTP_API intp_status sla_pack_slot_table(const uint8_t* slots, int64_t patch_cou
  * through `negative_l1_distance` (:233-241).                                  */
 INTP_API intp_status nl1_forward(const float* x, const float* w, float* out,
                         int64_t rows, int64_t protos, int64_t features, void* stream);
+
+/* Negative-L1 backward (float32, row-major contiguous; sign(0) = 0):
+ *   grad_x[m,f] = -sum_p grad_out[m,p] * sign(x[m,f] - w[p,f])
+ *   grad_w[p,f] =  sum_m grad_out[m,p] * sign(x[m,f] - w[p,f])
+ * Either output may be NULL.  Replaces `_negative_l1_backward_x/_w`
+ * (layers/triton_negative_l1.py:55-154, launched at :189-230).              */
+INTP_API intp_status nl1_backward(const float* x, const float* w, const float* grad_out, float* grad_x,
+                         float* grad_w, int64_t rows, int64_t protos, int64_t features, void* stream);
 
 /* Copies the device status word written by bounded waits to the host
  * (synchronous on `stream`) and clears it.  *code = 0 when no wait failed.  */

@@ -7,14 +7,17 @@ Public operators:
 The compute runs in ``_lib/libintp_b200.so`` (built by ``build.py``).
 """
 
-from .look_attention import LookSlots, check_device_status, look_attention_forward, structured_look_attention
-from .negative_l1 import negative_l1_distance, negative_l1_forward
+from .look_attention import (LookSlots, check_device_status, look_attention_backward, look_attention_forward,
+                             structured_look_attention)
+from .negative_l1 import negative_l1_backward, negative_l1_distance, negative_l1_forward
 
 __all__ = [
     "LookSlots",
     "check_device_status",
+    "look_attention_backward",
     "look_attention_forward",
     "structured_look_attention",
     "negative_l1_distance",
+    "negative_l1_backward",
     "negative_l1_forward",
 ]

@@ -31,9 +31,11 @@ SLA_KERNEL_AUTO, SLA_KERNEL_SIMT, SLA_KERNEL_TCGEN05 = 0, 1, 2
 # Every symbol include/intp_b200.h declares.
 EXPORTED_SYMBOLS = (
     "sla_forward",
+    "sla_backward",
     "sla_slot_table_bytes",
     "sla_pack_slot_table",
     "nl1_forward",
+    "nl1_backward",
     "sla_read_status",
     "sla_forward_noalloc",
     "intp_device_info",
@@ -77,6 +79,20 @@ class SlaForwardArgs(ctypes.Structure):
     ]
 
 
+class SlaBackwardArgs(ctypes.Structure):
+    """Mirror of ``sla_backward_args`` (field order and types must match)."""
+
+    _fields_ = [
+        ("fwd", SlaForwardArgs),
+        ("grad_out", _vp), ("grad_out_stride", _Stride),
+        ("grad_q", _vp), ("grad_k", _vp), ("grad_v", _vp),
+        ("grad_pose", _vp),
+        ("grad_fields", _vp),
+        ("grad_dense", _vp),
+        ("delta", _vp),
+    ]
+
+
 class SvitEmbedArgs(ctypes.Structure):
     """Mirror of ``svit_embed_args`` (include/intp_share_vit.h)."""
 
@@ -116,6 +132,10 @@ def load() -> ctypes.CDLL:
             raise NativeLibraryError(f"{LIB_PATH} lacks symbols {missing}")
         lib.sla_forward.argtypes = [ctypes.POINTER(SlaForwardArgs), _vp]
         lib.sla_forward.restype = _i32
+        lib.sla_backward.argtypes = [ctypes.POINTER(SlaBackwardArgs), _vp]
+        lib.sla_backward.restype = _i32
+        lib.nl1_backward.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]
+        lib.nl1_backward.restype = _i32
         lib.sla_slot_table_bytes.argtypes = [_i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]
         lib.sla_slot_table_bytes.restype = _i32
         lib.sla_pack_slot_table.argtypes = [_vp, _i64, _i32, _vp, _vp]

@@ -123,11 +123,21 @@ intp_status sla_pack_slot_table(const uint8_t* slots, int64_t patch_count, int32
   return INTP_OK;
 }
 
-intp_status sla_forward(const sla_forward_args* a, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Validates forward arguments (the reference's launch-site rules) and fills the
+// kernel parameter block.  INTP_OK with *empty set means there is no work.
+intp_status to_params(const sla_forward_args* a, intp::SlaParams* out, bool* empty) {
+  *empty = false;
   if (!a) return INTP_ERR_ARGUMENT;
   if (a->batch < 0 || a->heads < 0 || a->seq < 1 || a->head_dim < 1) return INTP_ERR_SHAPE;
   if (!valid_dtype(a->dtype)) return INTP_ERR_DTYPE;
-  if (a->batch == 0 || a->heads == 0) return INTP_OK;
+  if (a->batch == 0 || a->heads == 0) {
+    *empty = true;
+    return INTP_OK;
+  }
   if (!a->q || !a->k || !a->v || !a->out) return INTP_ERR_ARGUMENT;
   if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 || a->out_stride[3] != 1)
     return INTP_ERR_LAYOUT;
@@ -144,11 +154,7 @@ intp_status sla_forward(const sla_forward_args* a, void* stream) {
   if (a->dense && !valid_dtype(a->dense_dtype)) return INTP_ERR_DTYPE;
   if (a->kernel < SLA_KERNEL_AUTO || a->kernel > SLA_KERNEL_TCGEN05) return INTP_ERR_ARGUMENT;
 
-  DeviceFacts f;
-  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
-  if (f.major != 10) return INTP_ERR_ARCH;
-
-  intp::SlaParams p;
+  intp::SlaParams& p = *out;
   std::memset(&p, 0, sizeof(p));
   p.batch = a->batch;
   p.heads = a->heads;
@@ -179,11 +185,52 @@ intp_status sla_forward(const sla_forward_args* a, void* stream) {
   std::memcpy(p.dense_stride, a->dense_stride, sizeof(p.dense_stride));
   p.dense_dtype = a->dense_dtype;
   p.status = a->status;
+  return INTP_OK;
+}
 
+}  // namespace
+
+extern "C" {
+
+intp_status sla_forward(const sla_forward_args* a, void* stream) {
+  intp::SlaParams p;
+  bool empty = false;
+  const intp_status st = to_params(a, &p, &empty);
+  if (st != INTP_OK || empty) return st;
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (f.major != 10) return INTP_ERR_ARCH;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->kernel != SLA_KERNEL_SIMT && intp::sla_tc_supported(p)) return intp::launch_sla_tc(p, s, f.sms);
   if (a->kernel == SLA_KERNEL_TCGEN05) return INTP_ERR_UNSUPPORTED;
   return intp::launch_sla_simt(p, s);
+}
+
+intp_status sla_backward(const sla_backward_args* a, void* stream) {
+  if (!a) return INTP_ERR_ARGUMENT;
+  intp::SlaBwdParams bp;
+  std::memset(&bp, 0, sizeof(bp));
+  bool empty = false;
+  const intp_status st = to_params(&a->fwd, &bp.f, &empty);
+  if (st != INTP_OK || empty) return st;
+  if (!a->fwd.lse || !a->grad_out || !a->delta) return INTP_ERR_ARGUMENT;
+  if (a->grad_fields && a->fwd.bias_mode != SLA_BIAS_FIELDS) return INTP_ERR_ARGUMENT;
+  if (a->grad_pose && a->fwd.bias_mode == SLA_BIAS_NONE) return INTP_ERR_ARGUMENT;
+  if (a->grad_dense && !a->fwd.dense) return INTP_ERR_ARGUMENT;
+  if (a->fwd.seq < 2 && (a->grad_pose || a->grad_fields || a->grad_dense)) return INTP_ERR_SHAPE;
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (f.major != 10) return INTP_ERR_ARCH;
+  bp.grad_out = a->grad_out;
+  std::memcpy(bp.grad_out_stride, a->grad_out_stride, sizeof(bp.grad_out_stride));
+  bp.grad_q = a->grad_q;
+  bp.grad_k = a->grad_k;
+  bp.grad_v = a->grad_v;
+  bp.grad_pose = a->grad_pose;
+  bp.grad_fields = a->grad_fields;
+  bp.grad_dense = a->grad_dense;
+  bp.delta = a->delta;
+  return intp::launch_sla_backward(bp, static_cast<cudaStream_t>(stream));
 }
 
 intp_status nl1_forward(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
@@ -195,6 +242,18 @@ intp_status nl1_forward(const float* x, const float* w, float* out, int64_t rows
   if (!device_facts(&f)) return INTP_ERR_LAUNCH;
   if (f.major != 10) return INTP_ERR_ARCH;
   return intp::launch_nl1(x, w, out, rows, protos, features, static_cast<cudaStream_t>(stream));
+}
+
+intp_status nl1_backward(const float* x, const float* w, const float* grad_out, float* grad_x, float* grad_w,
+                         int64_t rows, int64_t protos, int64_t features, void* stream) {
+  if (rows < 0 || protos < 0 || features < 0) return INTP_ERR_SHAPE;
+  if (rows == 0 || protos == 0 || features == 0) return INTP_OK;
+  if (!x || !w || !grad_out || (!grad_x && !grad_w)) return INTP_ERR_ARGUMENT;
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (f.major != 10) return INTP_ERR_ARCH;
+  return intp::launch_nl1_backward(x, w, grad_out, grad_x, grad_w, rows, protos, features,
+                                   static_cast<cudaStream_t>(stream));
 }
 
 intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream) {

@@ -33,7 +33,23 @@ constexpr int kSlotTileQ = 128;
 constexpr int kSlotTileK = 64;
 constexpr int kSlotTileBytes = kSlotTileQ * kSlotTileK;
 
+// Backward pass parameters: the forward's (q, k, v, out = forward output,
+// lse = forward LSE, bias inputs) plus the output gradient and fp32 result
+// buffers (each may be null when not wanted).
+struct SlaBwdParams {
+  SlaParams f;
+  const void* grad_out; int64_t grad_out_stride[4];
+  float* grad_q; float* grad_k; float* grad_v;  // (B,H,N,D) contiguous
+  float* grad_pose;                              // (B,Np,H,P) contiguous
+  float* grad_fields;                            // (H,P,Np,Np) contiguous, zero-filled (FIELDS mode)
+  float* grad_dense;                             // (B,H,Np,Np) contiguous
+  float* delta;                                  // (B,H,N) scratch
+};
+
 int32_t launch_sla_simt(const SlaParams& p, cudaStream_t stream);
+int32_t launch_sla_backward(const SlaBwdParams& bp, cudaStream_t stream);
+int32_t launch_nl1_backward(const float* x, const float* w, const float* grad_out, float* grad_x, float* grad_w,
+                            int64_t rows, int64_t protos, int64_t features, cudaStream_t stream);
 // Returns INTP_ERR_UNSUPPORTED (8) when the tensor-core path does not apply.
 int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count);
 int32_t sla_tc_supported(const SlaParams& p);

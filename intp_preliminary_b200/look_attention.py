@@ -176,36 +176,10 @@ def _validate(q, k, v, pose, fields, dense_bias):
         raise ValueError("q, k and v must share a dtype")
 
 
-def look_attention_forward(
-    q: torch.Tensor,
-    k: torch.Tensor,
-    v: torch.Tensor,
-    pose: torch.Tensor,
-    fields,
-    *,
-    scale: float,
-    dense_bias: torch.Tensor | None = None,
-    want_lse: bool = False,
-    kernel: str = "auto",
-    out: torch.Tensor | None = None,
-):
-    """Forward only.  Returns ``(out, lse_or_None)``.
-
-    ``kernel`` selects the implementation: ``"auto"`` (tensor cores when the
-    inputs qualify, else CUDA cores), ``"simt"`` or ``"tcgen05"`` (raises if
-    the tensor-core path cannot take the inputs).
-    """
-    _validate(q, k, v, pose, fields, dense_bias)
+def _forward_args(q, k, v, pose, fields, scale, dense_bias, out, lse, kernel):
+    """``sla_forward_args`` for these tensors; also returns the temporaries it points at."""
     batch, heads, sequence, head_dim = q.shape
     device = q.device
-    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
-        raise ValueError("q, k, v need a unit stride on head_dim")
-    if out is None:
-        out = torch.empty((batch, heads, sequence, head_dim), dtype=q.dtype, device=device)
-    elif out.shape != q.shape or out.dtype != q.dtype or out.device != device or out.stride(-1) != 1:
-        raise ValueError("out must match q in shape, dtype and device with unit stride on head_dim")
-    lse = torch.empty((batch, heads, sequence), dtype=torch.float32, device=device) if want_lse else None
-
     args = _lib.SlaForwardArgs()
     args.batch, args.heads, args.seq, args.head_dim = batch, heads, sequence, head_dim
     args.scale = float(scale)
@@ -238,6 +212,40 @@ def look_attention_forward(
     if kernel not in _KERNELS:
         raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
     args.kernel = _KERNELS[kernel]
+    return args, keep
+
+
+def look_attention_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    pose: torch.Tensor,
+    fields,
+    *,
+    scale: float,
+    dense_bias: torch.Tensor | None = None,
+    want_lse: bool = False,
+    kernel: str = "auto",
+    out: torch.Tensor | None = None,
+):
+    """Forward only.  Returns ``(out, lse_or_None)``.
+
+    ``kernel`` selects the implementation: ``"auto"`` (tensor cores when the
+    inputs qualify, else CUDA cores), ``"simt"`` or ``"tcgen05"`` (raises if
+    the tensor-core path cannot take the inputs).
+    """
+    _validate(q, k, v, pose, fields, dense_bias)
+    batch, heads, sequence, head_dim = q.shape
+    device = q.device
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError("q, k, v need a unit stride on head_dim")
+    if out is None:
+        out = torch.empty((batch, heads, sequence, head_dim), dtype=q.dtype, device=device)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.device != device or out.stride(-1) != 1:
+        raise ValueError("out must match q in shape, dtype and device with unit stride on head_dim")
+    lse = torch.empty((batch, heads, sequence), dtype=torch.float32, device=device) if want_lse else None
+
+    args, keep = _forward_args(q, k, v, pose, fields, scale, dense_bias, out, lse, kernel)
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
@@ -246,21 +254,76 @@ def look_attention_forward(
     return out, lse
 
 
+def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale, dense_bias=None,
+                            needs=(True, True, True, True, True, True)):
+    """Gradients of ``look_attention_forward`` (flash-style, from the forward's
+    ``out`` and ``lse``).  Returns ``(dq, dk, dv, dpose, dfields, ddense)`` in the
+    inputs' dtypes; entries whose ``needs`` flag is False, ``dfields`` for
+    ``LookSlots`` fields (a table, not a tensor) and ``ddense`` without a dense
+    bias are None."""
+    _validate(q, k, v, pose, fields, dense_bias)
+    device = q.device
+    if grad_out.shape != q.shape or grad_out.device != device:
+        raise ValueError("grad_output must match q in shape and device")
+    grad_out = grad_out.to(q.dtype)
+    if grad_out.stride(-1) != 1:
+        grad_out = grad_out.contiguous()
+    batch, heads, sequence, head_dim = q.shape
+    patches = sequence - 1
+    slots = isinstance(fields, LookSlots)
+    f32 = dict(dtype=torch.float32, device=device)
+    dq = torch.empty(q.shape, **f32) if needs[0] else None
+    dk = torch.empty(q.shape, **f32) if needs[1] else None
+    dv = torch.empty(q.shape, **f32) if needs[2] else None
+    dpose = torch.empty(batch, patches, heads, pose.shape[-1], **f32) if needs[3] else None
+    dfields = torch.zeros(fields.shape, **f32) if needs[4] and not slots else None
+    ddense = torch.empty(batch, heads, patches, patches, **f32) if needs[5] and dense_bias is not None else None
+    delta = torch.empty(batch, heads, sequence, **f32)
+    fwd, keep = _forward_args(q, k, v, pose, fields, scale, dense_bias, out, lse, "simt")
+    args = _lib.SlaBackwardArgs()
+    args.fwd = fwd
+    args.grad_out, args.grad_out_stride = grad_out.data_ptr(), _stride4(grad_out)
+    for name, t in (("grad_q", dq), ("grad_k", dk), ("grad_v", dv), ("grad_pose", dpose), ("grad_fields", dfields),
+                    ("grad_dense", ddense), ("delta", delta)):
+        setattr(args, name, t.data_ptr() if t is not None else None)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        status = lib.sla_backward(ctypes.byref(args), ctypes.c_void_p(stream))
+    _lib.check(status, "structured Look attention backward")
+    del keep
+    return (dq.to(q.dtype) if dq is not None else None,
+            dk.to(k.dtype) if dk is not None else None,
+            dv.to(v.dtype) if dv is not None else None,
+            dpose.to(pose.dtype) if dpose is not None else None,
+            dfields.to(fields.dtype) if dfields is not None else None,
+            ddense.to(dense_bias.dtype) if ddense is not None else None)
+
+
 class _StructuredLookAttention(torch.autograd.Function):
-    """Autograd wrapper; the forward is the CUDA kernel, the backward is not built yet."""
+    """Autograd wrapper (layers/triton_structured_look_attention.py:297-409): the
+    forward keeps its LSE; the backward recomputes P from it on the GPU."""
 
     @staticmethod
     def forward(ctx, q, k, v, pose, fields, dense_bias, scale):
-        out, _ = look_attention_forward(
-            q, k, v, pose, fields, scale=scale, dense_bias=dense_bias if dense_bias.numel() else None
-        )
+        dense = dense_bias if dense_bias.numel() else None
+        out, lse = look_attention_forward(q, k, v, pose, fields, scale=scale, dense_bias=dense, want_lse=True)
+        ctx.scale = scale
+        ctx.slots = fields if isinstance(fields, LookSlots) else None
+        ctx.has_dense = dense is not None
+        saved_fields = fields if ctx.slots is None else q.new_empty(0)
+        ctx.save_for_backward(q, k, v, pose, saved_fields, dense_bias, out, lse)
         return out
 
     @staticmethod
     def backward(ctx, grad_output):
-        raise NotImplementedError(
-            "structured Look attention backward is not implemented on this build (forward/inference only)"
-        )
+        q, k, v, pose, fields, dense_bias, out, lse = ctx.saved_tensors
+        fields = ctx.slots if ctx.slots is not None else fields
+        needs = ctx.needs_input_grad[:6]
+        dq, dk, dv, dpose, dfields, ddense = look_attention_backward(
+            q, k, v, out, lse, grad_output, pose, fields, scale=ctx.scale,
+            dense_bias=dense_bias if ctx.has_dense else None, needs=needs)
+        return dq, dk, dv, dpose, dfields, ddense, None
 
 
 def structured_look_attention(q, k, v, pose, fields, *, scale, dense_bias=None):

@@ -51,16 +51,46 @@ def negative_l1_forward(x: torch.Tensor, prototype: torch.Tensor, *, out: torch.
     return out
 
 
+def negative_l1_backward(x: torch.Tensor, prototype: torch.Tensor, grad_output: torch.Tensor,
+                         needs=(True, True)):
+    """``(grad_x, grad_prototype)`` of ``-||x - w||_1`` (layers/triton_negative_l1.py:55-154,
+    189-230): with s = sign(x - w), sign(0) = 0, grad_x = -sum_p g s and
+    grad_w = sum_m g s, float32."""
+    _validate(x, prototype)
+    x = x.contiguous().float()
+    prototype = prototype.contiguous().float()
+    grad_output = grad_output.contiguous().float()
+    rows, features = x.shape
+    protos = prototype.shape[0]
+    if grad_output.shape != (rows, protos):
+        raise ValueError("grad_output must be (Q, P)")
+    gx = torch.empty_like(x) if needs[0] else None
+    gw = torch.empty_like(prototype) if needs[1] else None
+    if gx is None and gw is None:
+        return None, None
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        status = lib.nl1_backward(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(prototype.data_ptr()),
+            ctypes.c_void_p(grad_output.data_ptr()), ctypes.c_void_p(gx.data_ptr() if gx is not None else None),
+            ctypes.c_void_p(gw.data_ptr() if gw is not None else None), rows, protos, features,
+            ctypes.c_void_p(stream))
+    _lib.check(status, "negative L1 backward")
+    return gx, gw
+
+
 class _NegativeL1(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, prototype):
+        ctx.save_for_backward(x, prototype)
         return negative_l1_forward(x, prototype)
 
     @staticmethod
     def backward(ctx, grad_output):
-        raise NotImplementedError(
-            "negative L1 backward is not implemented on this build (forward/inference only)"
-        )
+        x, prototype = ctx.saved_tensors
+        gx, gw = negative_l1_backward(x, prototype, grad_output, needs=ctx.needs_input_grad[:2])
+        return (gx.to(x.dtype) if gx is not None else None, gw.to(prototype.dtype) if gw is not None else None)
 
 
 def negative_l1_distance(x: torch.Tensor, prototype: torch.Tensor) -> torch.Tensor:

@@ -62,6 +62,15 @@ def _synthetic_case(ref_fn, lattice, *, rows, cols, n_dir, n_rad, batch, heads, 
         onehot[p] = (table == p).float()
     fields = onehot.unsqueeze(0).expand(heads, -1, -1, -1)
     out = ref_fn(q, k, v, pose, fields, scale=1 / math.sqrt(dim))
+    grads = {}
+    if dtype == torch.float32:
+        # gradients through the reference's one-hot form: d out / d (q, k, v, per-slot pose)
+        leaves = [t.detach().clone().requires_grad_(True) for t in (q, k, v, pose)]
+        o = ref_fn(*leaves, fields, scale=1 / math.sqrt(dim))
+        go = torch.randn(o.shape, generator=g)
+        o.backward(go)
+        grads = {"grad_out": go.numpy(), **{f"grad_{n}": t.grad.numpy() for n, t in zip(("q", "k", "v", "pose"), leaves)}}
+
     def raw(t):
         # bf16 inputs are stored as their 16-bit patterns to halve the fixture size
         return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
@@ -69,7 +78,7 @@ def _synthetic_case(ref_fn, lattice, *, rows, cols, n_dir, n_rad, batch, heads, 
     return {
         "q": raw(q), "k": raw(k), "v": raw(v),
         "pose": pose.numpy(), "slots": slots, "out": out.float().numpy(),
-        "scale": np.float64(1 / math.sqrt(dim)), "n_slots": np.int64(n_slots),
+        "scale": np.float64(1 / math.sqrt(dim)), "n_slots": np.int64(n_slots), **grads,
     }
 
 
@@ -104,6 +113,19 @@ def main() -> None:
         look[f"p{poses}_scale"] = np.float64(scale)
         half = [t.half() for t in tensors]
         look[f"p{poses}_out_half"] = ref_attn(*half, scale=scale).float().numpy()
+        # all gradients, as tests/test_triton_structured_look_attention.py:23-57 checks them
+        torch.manual_seed(1700 + poses)
+        grad_out = torch.randn(out.shape)
+        look[f"p{poses}_grad_out"] = grad_out.numpy()
+        for tag, with_dense in (("", False), ("_dense", True)):
+            leaves = [t.detach().clone().requires_grad_(True) for t in tensors]
+            dense_leaf = dense.detach().clone().requires_grad_(True)
+            o = ref_attn(*leaves, scale=scale, dense_bias=dense_leaf if with_dense else None)
+            o.backward(grad_out)
+            for name, t in zip(("q", "k", "v", "pose", "fields"), leaves):
+                look[f"p{poses}_grad{tag}_{name}"] = t.grad.numpy()
+            if with_dense:
+                look[f"p{poses}_grad_dense_dense"] = dense_leaf.grad.numpy()
     cfg1 = _synthetic_case(ref_attn, hex_lattice, rows=14, cols=14, n_dir=12, n_rad=4,
                            batch=1, heads=3, dim=64, dtype=torch.float32, seed=1)
     for key, value in cfg1.items():
@@ -124,6 +146,13 @@ def main() -> None:
         nl1[f"{name}_x"] = x.numpy()
         nl1[f"{name}_w"] = w.numpy()
         nl1[f"{name}_out"] = ref_nl1(x, w).numpy()
+        xl, wl = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+        out = ref_nl1(xl, wl)
+        go = torch.randn(out.shape, generator=g)
+        out.backward(go)
+        nl1[f"{name}_grad_out"] = go.numpy()
+        nl1[f"{name}_grad_x"] = xl.grad.numpy()
+        nl1[f"{name}_grad_w"] = wl.grad.numpy()
     np.savez_compressed(HERE / "negative_l1_reference.npz", **nl1)
 
     # --- hex geometry ---------------------------------------------------------------

@@ -59,6 +59,14 @@ def test_abi_version_and_status_strings():
     assert "timed out" in _lib.status_string(_lib.INTP_ERR_TIMEOUT)
 
 
+def test_backward_struct_layout_matches_header_field_order():
+    text = HEADER.read_text()
+    body = text[text.index("typedef struct sla_backward_args"):text.index("} sla_backward_args;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = re.findall(r"(\w+)(?:\[4\])?\s*[;,]", body)
+    assert names == [f[0] for f in _lib.SlaBackwardArgs._fields_]
+
+
 def test_struct_layout_matches_header_field_order():
     text = HEADER.read_text()
     body = text[text.index("typedef struct sla_forward_args"):text.index("} sla_forward_args;")]
