@@ -146,6 +146,98 @@ struct TcArgs {
   int32_t pose_vec4;      // pose rows are 16-byte aligned fp32 with unit slot stride
 };
 
+// Per-query Look values of query token i into column `row` of the [slot][row]
+// table (bank = row % 32: conflict free), pre-scaled to the log2 domain, plus
+// the "no bias" (0) and "past the end" (-inf) entries.  Only this thread reads
+// its column.
+__device__ __forceinline__ void stage_table(float* table_s, const TcArgs& a, int64_t b, int64_t h, int64_t i,
+                                            int row) {
+  const SlaParams& p = a.p;
+  const int32_t ns = a.n_slots;
+  const bool valid = i >= 1 && i < p.seq;
+  const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
+  if (a.pose_vec4) {
+    // Eight 16-byte loads in flight per batch: one memory round trip per 32 slots.
+    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
+    for (int s0 = 0; s0 < ns / 4; s0 += 8) {
+      float4 v4[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v4[u] = (valid && s0 + u < ns / 4) ? __ldg(src + s0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u < ns / 4) {
+          float* dst = table_s + 4 * (s0 + u) * BM + row;
+          dst[0] = v4[u].x * kLog2e;
+          dst[BM] = v4[u].y * kLog2e;
+          dst[2 * BM] = v4[u].z * kLog2e;
+          dst[3 * BM] = v4[u].w * kLog2e;
+        }
+      }
+    }
+  } else {
+    for (int s = 0; s < ns; ++s)
+      table_s[s * BM + row] = valid ? load_any(p.pose, base + s * p.pose_stride[3], p.pose_dtype) * kLog2e : 0.f;
+  }
+  table_s[ns * BM + row] = 0.f;               // "no bias"
+  table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
+}
+
+// S row (64 fp32 scores of this thread's TMEM lane) into t[c] = keys 2c, 2c+1.
+__device__ __forceinline__ void load_s_row(uint32_t s_addr, float2 (&t)[BN / 2]) {
+  uint32_t r0[16], r1[16], r2[16], r3[16];
+  tmem_ld16(s_addr, r0);
+  tmem_ld16(s_addr + 16, r1);
+  tmem_ld16(s_addr + 32, r2);
+  tmem_ld16(s_addr + 48, r3);
+  tmem_wait_ld();
+  reg_fence16(r0);
+  reg_fence16(r1);
+  reg_fence16(r2);
+  reg_fence16(r3);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    t[e] = make_float2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]));
+    t[8 + e] = make_float2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]));
+    t[16 + e] = make_float2(__uint_as_float(r2[2 * e]), __uint_as_float(r2[2 * e + 1]));
+    t[24 + e] = make_float2(__uint_as_float(r3[2 * e]), __uint_as_float(r3[2 * e + 1]));
+  }
+}
+
+// t = scale*log2(e)*s + bias (log2 domain): slot bytes from the packed tile row,
+// per-query values from the [slot][row] table.
+__device__ __forceinline__ void add_look_bias(float2 (&t)[BN / 2], const uint8_t* srow, const float* trow,
+                                              float scale_log2) {
+#pragma unroll
+  for (int c = 0; c < BN / 16; ++c) {
+    const uint4 w = *reinterpret_cast<const uint4*>(srow + c * 2048);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      const uint32_t s0 = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
+      const uint32_t s1 = __byte_perm(ww[e >> 2], 0u, 0x4440u | ((e + 1) & 3));
+      float2& tv = t[c * 8 + e / 2];
+      tv.x = fmaf(tv.x, scale_log2, trow[s0 * BM]);
+      tv.y = fmaf(tv.y, scale_log2, trow[s1 * BM]);
+    }
+  }
+}
+
+// The constant "ones" tile: 64 keys x 64 columns (16-bit) in the 128B-swizzled
+// layout TMA gives V, logical column 0 = 1, every other column 0.  Written by
+// 128 threads (thread index `tid`).
+template <bool BF16>
+__device__ __forceinline__ void fill_ones_tile(uint8_t* ones_s, int tid) {
+  const uint16_t one = BF16 ? uint16_t(0x3F80) : uint16_t(0x3C00);
+  for (int w = tid; w < static_cast<int>(kKVBytes / 16); w += 128) {
+    const int r = w >> 3, chunk = w & 7;  // 16-byte chunk `chunk` of key row r
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (chunk == (r & 7)) v.x = one;      // logical chunk 0 lands at physical chunk r % 8
+    reinterpret_cast<uint4*>(ones_s)[w] = v;
+  }
+  fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor core
+}
+
 template <int KS, bool BF16>
 __global__ void __launch_bounds__(kThreads, 2)
 sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -189,18 +281,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     bars->abort = 0;
     mbar_fence_init();
   }
-  // The ones tile: a 64-key x 64-column bf16/f16 block in the same 128B-swizzled
-  // layout TMA gives V, with logical column 0 equal to 1 and every other column 0.
-  if (warp < 4) {
-    const uint16_t one = BF16 ? uint16_t(0x3F80) : uint16_t(0x3C00);
-    for (int w = threadIdx.x; w < static_cast<int>(kKVBytes / 16); w += 128) {
-      const int r = w >> 3, chunk = w & 7;  // 16-byte chunk `chunk` of key row r
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (chunk == (r & 7)) v.x = one;      // logical chunk 0 lands at physical chunk r % 8
-      reinterpret_cast<uint4*>(ones_s)[w] = v;
-    }
-    fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor core
-  }
+  if (warp < 4) fill_ones_tile<BF16>(ones_s, threadIdx.x);
   if (warp == 5) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
@@ -379,7 +460,6 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const int row = threadIdx.x;  // 0..127, TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const float scale_log2 = p.scale * kLog2e;  // > 0 (checked on the host)
-    const int32_t ns = a.n_slots;
     uint32_t k_iter = 0;
     uint32_t g = 0;  // global index of the key tile being processed (S/P buffer g & 1)
     // Waits until the PV MMA of global tile t (buffer t & 1) has completed.
@@ -392,38 +472,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       const uint32_t bh = item / n_qt;
       const int64_t h = bh % H, b = bh / H;
       const int64_t i = static_cast<int64_t>(qt) * BM + row;  // token index of this thread's row
-      if (use_bias) {
-        // Per-query Look values, [slot][row] layout (bank = row % 32: conflict
-        // free), pre-scaled to the log2 domain.  Only this thread reads its column.
-        const bool valid = i >= 1 && i < N;
-        const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
-        if (a.pose_vec4) {
-          // Eight 16-byte loads in flight per batch: one memory round trip per 32 slots.
-          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
-          for (int s0 = 0; s0 < ns / 4; s0 += 8) {
-            float4 v4[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              v4[u] = (valid && s0 + u < ns / 4) ? __ldg(src + s0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              if (s0 + u < ns / 4) {
-                float* dst = table_s + 4 * (s0 + u) * BM + row;
-                dst[0] = v4[u].x * kLog2e;
-                dst[BM] = v4[u].y * kLog2e;
-                dst[2 * BM] = v4[u].z * kLog2e;
-                dst[3 * BM] = v4[u].w * kLog2e;
-              }
-            }
-          }
-        } else {
-          for (int s = 0; s < ns; ++s)
-            table_s[s * BM + row] =
-                valid ? load_any(p.pose, base + s * p.pose_stride[3], p.pose_dtype) * kLog2e : 0.f;
-        }
-        table_s[ns * BM + row] = 0.f;               // "no bias"
-        table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
-      }
+      if (use_bias) stage_table(table_s, a, b, h, i, row);
       float m = -INFINITY;
       uint64_t tile_mask = 0;  // bit k: key tile (j & ~63) + k carries Look bias for this warp
       for (int64_t j = 0; j < n_kt; ++j, ++k_iter) {
@@ -443,25 +492,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         tc_fence_after();
         const uint32_t s_addr = lane_base + (sb ? kColS1 : kColS0);
         float2 t[BN / 2];  // t[c] holds keys 2c and 2c+1
-        {
-          uint32_t r0[16], r1[16], r2[16], r3[16];
-          tmem_ld16(s_addr, r0);
-          tmem_ld16(s_addr + 16, r1);
-          tmem_ld16(s_addr + 32, r2);
-          tmem_ld16(s_addr + 48, r3);
-          tmem_wait_ld();
-          reg_fence16(r0);
-          reg_fence16(r1);
-          reg_fence16(r2);
-          reg_fence16(r3);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            t[e] = make_float2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]));
-            t[8 + e] = make_float2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]));
-            t[16 + e] = make_float2(__uint_as_float(r2[2 * e]), __uint_as_float(r2[2 * e + 1]));
-            t[24 + e] = make_float2(__uint_as_float(r3[2 * e]), __uint_as_float(r3[2 * e + 1]));
-          }
-        }
+        load_s_row(s_addr, t);
 
         // t holds raw scores on tiles without Look bias, and the log2-domain
         // logits scale*log2(e)*s + bias on tiles with it.
@@ -472,21 +503,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             ok = false;
             break;
           }
-          const uint8_t* srow = slot_s + st * kSlotBytes + row * 16;
-          const float* trow = table_s + row;
-#pragma unroll
-          for (int c = 0; c < BN / 16; ++c) {
-            const uint4 w = *reinterpret_cast<const uint4*>(srow + c * 2048);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              const uint32_t s0 = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
-              const uint32_t s1 = __byte_perm(ww[e >> 2], 0u, 0x4440u | ((e + 1) & 3));
-              float2& tv = t[c * 8 + e / 2];
-              tv.x = fmaf(tv.x, scale_log2, trow[s0 * BM]);
-              tv.y = fmaf(tv.y, scale_log2, trow[s1 * BM]);
-            }
-          }
+          add_look_bias(t, slot_s + st * kSlotBytes + row * 16, table_s + row, scale_log2);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->k_empty[st]);
@@ -751,10 +768,10 @@ int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
       cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&regs_per_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess)
     return 6;
+  const bool bf16 = p.dtype == 2;
   // Three K / slot-tile stages when two CTAs still fit on an SM, else two.
   const size_t smem3 = smem_bytes_for<3>(a.table_bytes), smem2 = smem_bytes_for<2>(a.table_bytes);
   const bool three = 2 * (smem3 + 1024) <= static_cast<size_t>(smem_per_sm);
-  const bool bf16 = p.dtype == 2;
   if (three)
     return bf16 ? launch_variant<3, true>(mq, mk, mv, a, smem3, smem_per_sm, regs_per_sm, sm_count, stream)
                 : launch_variant<3, false>(mq, mk, mv, a, smem3, smem_per_sm, regs_per_sm, sm_count, stream);
