@@ -18,6 +18,8 @@
  *                         per-query Look values the attention kernel reads.
  *   svit_add_layernorm  : residual add + LayerNorm + bf16 cast of the
  *                         pre-norm transformer block (layers/mini_vit.py:138-170).
+ *   svit_linear_gelu,   : the block's linear layers on tcgen05 with GELU, or
+ *   svit_linear_residual_layernorm   residual add + next LayerNorm, in the epilogue.
  * Same conventions as intp_b200.h: device pointers, element strides, a CUDA
  * stream, intp_status return codes; nothing is allocated or freed.
  */
@@ -74,6 +76,28 @@ INTP_API intp_status svit_embed_post(const svit_embed_args* args, void* stream);
 INTP_API intp_status svit_add_layernorm(float* x, int64_t x_stride, const void* y, int64_t y_stride,
                                         const float* gamma, const float* beta, float eps, int64_t rows,
                                         int64_t dim, void* h, int64_t h_stride, void* stream);
+
+/* Linear layers of the transformer block on tcgen05 tensor cores with the
+ * element-wise work that follows them fused into the epilogue
+ * (layers/mini_vit.py:138-170: fc1 -> GELU; proj / fc2 -> residual add ->
+ * next pre-norm).  C = A W^T + bias with A (rows, in_features) bf16 (row
+ * stride a_stride, 16-byte aligned rows), W (out_features, in_features) bf16
+ * contiguous (a torch Linear weight), bias float32; fp32 accumulation.
+ * in_features % 64 == 0.  `status` is the device int32 that bounded waits
+ * write on failure (as in sla_forward_args.status).
+ *
+ * svit_linear_gelu: out = bf16(GELU(C)) with the exact error function
+ *   (nn.GELU()); out_features % 256 == 0; out row stride % 8 == 0.
+ * svit_linear_residual_layernorm: x += C (x float32, updated in place), then
+ *   h = bf16(LayerNorm(x) * gamma + beta); dim (= out_features) == 192.     */
+INTP_API intp_status svit_linear_gelu(const void* a, int64_t a_stride, int64_t rows, int32_t in_features,
+                                      const void* weight, const float* bias, int32_t out_features, void* out,
+                                      int64_t out_stride, int32_t* status, void* stream);
+INTP_API intp_status svit_linear_residual_layernorm(const void* a, int64_t a_stride, int64_t rows,
+                                                    int32_t in_features, const void* weight, const float* bias,
+                                                    int32_t dim, float* x, int64_t x_stride, const float* gamma,
+                                                    const float* beta, float eps, void* h, int64_t h_stride,
+                                                    int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -47,6 +47,8 @@ SHARE_VIT_SYMBOLS = (
     "svit_gather_patches",
     "svit_embed_post",
     "svit_add_layernorm",
+    "svit_linear_gelu",
+    "svit_linear_residual_layernorm",
 )
 
 _i64 = ctypes.c_int64
@@ -154,6 +156,11 @@ def load() -> ctypes.CDLL:
         lib.svit_embed_post.restype = _i32
         lib.svit_add_layernorm.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, ctypes.c_float, _i64, _i64, _vp, _i64, _vp]
         lib.svit_add_layernorm.restype = _i32
+        lib.svit_linear_gelu.argtypes = [_vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp]
+        lib.svit_linear_gelu.restype = _i32
+        lib.svit_linear_residual_layernorm.argtypes = [_vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp,
+                                                       ctypes.c_float, _vp, _i64, _vp, _vp]
+        lib.svit_linear_residual_layernorm.restype = _i32
         lib.intp_abi_version.argtypes = []
         lib.intp_abi_version.restype = _i32
         lib.intp_status_string.argtypes = [_i32]

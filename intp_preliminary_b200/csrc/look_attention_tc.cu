@@ -34,6 +34,7 @@
 #include <cstdint>
 #include "sla_internal.h"
 #include "sm100_ptx.cuh"
+#include "tma_host.h"
 
 namespace intp {
 namespace {
@@ -615,23 +616,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------- host side
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
+EncodeTiledFn get_encode_fn() { return tensor_map_encoder(); }
 
 // Builds a 4-D map (head_dim, then row / head / batch sorted by stride) over a
 // (B, H, N, D) tensor with element strides `stride`, and reports where each

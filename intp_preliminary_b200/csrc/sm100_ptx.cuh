@@ -134,6 +134,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* desc, uint64_
       : "memory");
 }
 
+// 2-D tiled tensor load into shared memory, completion on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* desc, uint64_t* bar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(desc), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 // Plain (untiled) bulk copy global -> shared, 16-byte aligned, size % 16 == 0.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

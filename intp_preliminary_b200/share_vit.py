@@ -48,7 +48,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .look_attention import LookSlots, look_attention_forward
-from .share_vit_ops import add_layernorm, embed_post, gather_patches
+from .share_vit_ops import add_layernorm, embed_post, gather_patches, linear_gelu, linear_residual_layernorm
 
 IMAGE_SIZE = 224
 IN_CHANS = 3
@@ -477,12 +477,19 @@ class ShareViTHalf6d3r(nn.Module):
         return x, values.permute(0, 2, 1, 3)
 
     @torch.no_grad()
-    def trunk_fused(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool = False) -> torch.Tensor:
-        """The 12 blocks and the final LayerNorm in bf16 on the fused kernels:
-        add + LayerNorm + cast in one pass, cuBLAS linears (bias in the epilogue),
-        Look attention writing token-major output.  ``x`` is updated in place.
-        Returns the normalised tokens (B, N+1, 192) bf16, or only the CLS rows
-        (B, 192) when ``cls_only``."""
+    def trunk_fused(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool = False,
+                    linears: str = "tcgen05") -> torch.Tensor:
+        """The 12 blocks and the final LayerNorm in bf16 on the fused kernels.
+        ``linears="tcgen05"``: proj and fc2 are tcgen05 GEMMs whose epilogue adds
+        the residual and applies the next LayerNorm, fc1 one whose epilogue applies
+        GELU (qkv stays a cuBLAS GEMM).  ``linears="cublas"``: cuBLAS linears with
+        separate add + LayerNorm and GELU passes.  Look attention writes
+        token-major output.  ``x`` is updated in place.  Returns the normalised
+        tokens (B, N+1, 192) bf16, or only the CLS rows (B, 192) when ``cls_only``."""
+        if linears not in ("tcgen05", "cublas"):
+            raise ValueError("linears must be 'tcgen05' or 'cublas'")
+        if linears == "tcgen05":
+            return self._trunk_tcgen05(x, values, cls_only=cls_only)
         batch, n1 = x.shape[0], x.shape[1]
         rows = batch * n1
         head_dim = EMBED_DIM // HEADS
@@ -511,6 +518,37 @@ class ShareViTHalf6d3r(nn.Module):
         if cls_only:
             return add_layernorm(x[:, 0], y.view(batch, n1, EMBED_DIM)[:, 0], self.norm.weight, self.norm.bias, 1e-6)
         return add_layernorm(x, y, self.norm.weight, self.norm.bias, 1e-6).view(batch, n1, EMBED_DIM)
+
+    def _trunk_tcgen05(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool) -> torch.Tensor:
+        batch, n1 = x.shape[0], x.shape[1]
+        rows = batch * n1
+        head_dim = EMBED_DIM // HEADS
+        weights = self._trunk_weights(torch.bfloat16)
+        scale = 1.0 / math.sqrt(head_dim)
+        events = self.attention_events
+        attn = torch.empty(batch, n1, HEADS, head_dim, dtype=torch.bfloat16, device=x.device)
+        attn_bhnd = attn.permute(0, 2, 1, 3)
+        xr = x.view(rows, EMBED_DIM)
+        h = add_layernorm(x, None, self.blocks[0].norm1.weight, self.blocks[0].norm1.bias, 1e-6)
+        for layer, blk in enumerate(self.blocks):
+            w_qkv, b_qkv, w_proj, _, w_fc1, _, w_fc2, _ = weights[layer]
+            qkv = F.linear(h, w_qkv, b_qkv).view(batch, n1, 3, HEADS, head_dim)
+            q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+            pose_l = values[:, :, HEADS * layer:HEADS * (layer + 1)]
+            if events is not None:
+                start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+            look_attention_forward(q, k, v, pose_l, self.look_slots, scale=scale, out=attn_bhnd)
+            if events is not None:
+                stop.record()
+                events.append((start, stop))
+            h = linear_residual_layernorm(attn.view(rows, EMBED_DIM), w_proj, blk.attn.proj.bias, xr,
+                                          blk.norm2.weight, blk.norm2.bias, 1e-6)
+            u = linear_gelu(h, w_fc1, blk.mlp.fc1.bias)
+            nxt = self.blocks[layer + 1].norm1 if layer + 1 < len(self.blocks) else self.norm
+            h = linear_residual_layernorm(u, w_fc2, blk.mlp.fc2.bias, xr, nxt.weight, nxt.bias, 1e-6)
+        h = h.view(batch, n1, EMBED_DIM)
+        return h[:, 0] if cls_only else h
 
     def slot_fields(self) -> torch.Tensor:
         """F[h, p, s] = sum_g basis[p, g, s] * grid[h, g]: the Look field value of

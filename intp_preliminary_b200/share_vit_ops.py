@@ -113,3 +113,58 @@ def add_layernorm(x: torch.Tensor, y: torch.Tensor | None, weight: torch.Tensor,
         float(eps), rows, dim, _ptr(outr), outr.stride(0), _stream(x.device))
     _lib.check(status, "add + LayerNorm")
     return out
+
+
+def _linear_checks(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    _require(a.is_cuda and a.dtype == torch.bfloat16 and a.ndim == 2 and a.stride(1) == 1,
+             "input must be a bf16 CUDA matrix with unit column stride")
+    _require(weight.dtype == torch.bfloat16 and weight.is_contiguous() and weight.ndim == 2
+             and weight.shape[1] == a.shape[1] and weight.device == a.device,
+             "weight must be a contiguous bf16 (out_features, in_features) tensor on the input's device")
+    _require(bias.dtype == torch.float32 and bias.is_contiguous() and bias.shape == (weight.shape[0],)
+             and bias.device == a.device, "bias must be a contiguous float32 (out_features,) tensor")
+    _require(a.shape[1] % 64 == 0, "in_features must be a multiple of 64")
+    return a
+
+
+def _status(device: torch.device) -> ctypes.c_void_p:
+    from .look_attention import _status_word
+
+    return ctypes.c_void_p(_status_word(device).data_ptr())
+
+
+def linear_gelu(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """``bf16(GELU(a @ weight.T + bias))`` (exact erf GELU) on the tcgen05 GEMM with
+    the activation in its epilogue.  a (rows, K) bf16, weight (N, K) bf16, bias (N,) fp32."""
+    _linear_checks(a, weight, bias)
+    rows, k = a.shape
+    n = weight.shape[0]
+    _require(n % 256 == 0, "out_features must be a multiple of 256")
+    out = torch.empty(rows, n, dtype=torch.bfloat16, device=a.device)
+    status = _lib.load().svit_linear_gelu(_ptr(a), a.stride(0), rows, k, _ptr(weight), _ptr(bias), n, _ptr(out),
+                                          out.stride(0), _status(a.device), _stream(a.device))
+    _lib.check(status, "linear + GELU")
+    return out
+
+
+def linear_residual_layernorm(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, x: torch.Tensor,
+                              norm_weight: torch.Tensor, norm_bias: torch.Tensor, eps: float) -> torch.Tensor:
+    """``x += a @ weight.T + bias`` (x float32, in place) and return
+    ``bf16(LayerNorm(x))``, from one tcgen05 GEMM with the residual add and the
+    LayerNorm in its epilogue.  dim = weight.shape[0] = 192."""
+    _linear_checks(a, weight, bias)
+    rows, k = a.shape
+    dim = weight.shape[0]
+    _require(x.dtype == torch.float32 and x.device == a.device and x.shape[-1] == dim and x.stride(-1) == 1,
+             "x must be float32 with unit last stride and dim columns")
+    xr = x.reshape(-1, dim)
+    _require(xr.data_ptr() == x.data_ptr() and xr.shape[0] == rows, "x rows must match the input rows")
+    for t in (norm_weight, norm_bias):
+        _require(t.dtype == torch.float32 and t.is_contiguous() and t.shape == (dim,) and t.device == a.device,
+                 "LayerNorm weight and bias must be contiguous float32 (dim,)")
+    h = torch.empty(rows, dim, dtype=torch.bfloat16, device=a.device)
+    status = _lib.load().svit_linear_residual_layernorm(
+        _ptr(a), a.stride(0), rows, k, _ptr(weight), _ptr(bias), dim, _ptr(xr), xr.stride(0), _ptr(norm_weight),
+        _ptr(norm_bias), float(eps), _ptr(h), h.stride(0), _status(a.device), _stream(a.device))
+    _lib.check(status, "linear + residual + LayerNorm")
+    return h

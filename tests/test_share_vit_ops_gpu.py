@@ -83,3 +83,42 @@ def test_fused_forward_matches_unfused_bf16(model, cuda_device):
     assert fused.shape == (6, 100) and torch.isfinite(fused).all()
     feats_fused = model.forward_features(images)
     assert feats_fused.shape == (6, 196, EMBED_DIM)
+
+
+@pytest.mark.parametrize("rows", [1, 130, 4096 + 77])
+def test_linear_gelu_matches_torch(cuda_device, rows):
+    g = torch.Generator(cuda_device).manual_seed(rows)
+    a = (torch.randn(rows, 192, device=cuda_device, generator=g)).to(torch.bfloat16)
+    w = (torch.randn(768, 192, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+    b = torch.randn(768, device=cuda_device, generator=g) * 0.1
+    out = ops.linear_gelu(a, w, b)
+    ref = F.gelu(a.float() @ w.float().t() + b)
+    assert out.dtype == torch.bfloat16 and out.shape == (rows, 768)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("rows,k", [(1, 192), (130, 192), (4096 + 77, 768)])
+def test_linear_residual_layernorm_matches_torch(cuda_device, rows, k):
+    g = torch.Generator(cuda_device).manual_seed(rows + k)
+    a = torch.randn(rows, k, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(192, k, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+    b = torch.randn(192, device=cuda_device, generator=g) * 0.1
+    x = torch.randn(rows, 192, device=cuda_device, generator=g)
+    nw = torch.randn(192, device=cuda_device, generator=g)
+    nb = torch.randn(192, device=cuda_device, generator=g)
+    x_ref = x + (a.float() @ w.float().t() + b)
+    h_ref = F.layer_norm(x_ref, (192,), nw, nb, 1e-6)
+    h = ops.linear_residual_layernorm(a, w, b, x, nw, nb, 1e-6)
+    torch.testing.assert_close(x, x_ref, atol=1e-3, rtol=1e-4)
+    torch.testing.assert_close(h.float(), h_ref, atol=3e-2, rtol=1e-2)
+
+
+def test_tcgen05_linears_match_cublas_trunk(model, cuda_device):
+    images = torch.randn(5, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(11))
+    x1, values = model.embed_fused(images)
+    x2 = x1.clone()
+    fused = model.trunk_fused(x1, values, linears="tcgen05").float()
+    plain = model.trunk_fused(x2, values, linears="cublas").float()
+    err = (fused - plain).abs().max().item()
+    assert err <= 5e-2 * plain.abs().max().item(), err
+    assert torch.isfinite(fused).all()
