@@ -11,10 +11,11 @@
 // CTA (one per SM, persistent over 128-row x NT-column tiles): warp 0 issues
 // TMA loads of 64-wide K slabs of A and W into a STAGES-deep ring (128-byte
 // swizzle); warp 1 issues tcgen05.mma (M = 128, N = NT, K = 16 per
-// instruction) into one of two TMEM accumulators; warpgroups 1 and 2 (warps
-// 4-7, 8-11) take alternate tiles and run the epilogue from TMEM, one row per
-// thread, while the next tile accumulates in the other buffer.  Every wait is
-// bounded (sm100_ptx.cuh).
+// instruction) into one of two TMEM accumulators; two groups of four
+// epilogue warps (2-5, 6-9: warp w reads TMEM lanes 32 (w % 4) .. + 31) take
+// alternate tiles and run the epilogue from TMEM, one row per thread, while
+// the next tile accumulates in the other buffer.  Every wait is bounded
+// (sm100_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cstdint>
@@ -28,9 +29,18 @@ namespace {
 constexpr int kGBM = 128;                          // rows per tile
 constexpr int kGBK = 64;                           // K per slab: 128 bytes of bf16 = one swizzle atom
 constexpr uint32_t kASlab = kGBM * kGBK * 2;       // 16 KB
-constexpr int kGemmThreads = 384;                  // warps 0 (TMA), 1 (MMA), 2-3 idle, 4-11 epilogue
+// Warps: 0 TMA, 1 MMA, then groups of four epilogue warps.  Two groups per
+// accumulator buffer for GELU (each takes half of the tile's columns), one for
+// LayerNorm (a row's statistics stay inside one thread).
+template <int EPI>
+__host__ __device__ constexpr int epi_groups_per_tile() { return EPI == 0 ? 2 : 1; }
+template <int EPI>
+__host__ __device__ constexpr int gemm_threads() { return 64 + 2 * epi_groups_per_tile<EPI>() * 128; }
 constexpr int kEpiGelu = 0, kEpiResidualLN = 1;
-constexpr int kStageWords = 32 * 33;     // per epilogue warp: 32 rows x 32 columns, pitch 33
+// Per epilogue warp, in 32-bit words: GELU two 32 x 32 bf16 blocks; LN two 32 x 32 fp32 residual chunks.
+template <int EPI>
+__host__ __device__ constexpr int stage_words() { return EPI == 0 ? 1024 : 2048; }
+constexpr int kMaxGeluN = 4096;         // GELU bias columns kept in shared memory
 constexpr uint32_t kBarrierBytes = 256;  // room reserved for the barrier block
 
 struct GemmArgs {
@@ -60,11 +70,300 @@ struct GemmBarriers {
   int32_t abort;
 };
 
-// GELU with the exact error function, as nn.GELU() computes it.
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
+// GELU with the error function (nn.GELU(), not its tanh approximation), for
+// two columns at once on the packed fp32 pipe.
+//
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula
+// 7.1.28: for z >= 0, erf(z) = 1 - (1 + a1 z + ... + a6 z^6)^-16, |error| <=
+// 3e-7 (about 2e-6 in fp32 arithmetic) - far below the bf16 resolution of the
+// output.  With z = |v| / sqrt(2) and q = (1 + ... )^-16 = erfc(z):
+//   GELU(v) = v (1 + erf(v / sqrt 2)) / 2 = max(v, 0) - |v| q / 2
+// for either sign of v.  One reciprocal (MUFU) per column; the sqrt(2) is
+// folded into the coefficients (c_k = a_k 2^(-k/2)).  NaN propagates.
+constexpr float kErfC1 = 0.0705230784f * 0.70710678118654752f;
+constexpr float kErfC2 = 0.0422820123f * 0.5f;
+constexpr float kErfC3 = 0.0092705272f * 0.35355339059327376f;
+constexpr float kErfC4 = 0.0001520143f * 0.25f;
+constexpr float kErfC5 = 0.0002765672f * 0.17677669529663688f;
+constexpr float kErfC6 = 0.0000430638f * 0.125f;
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
+
+__device__ __forceinline__ uint32_t gelu_bf16x2(float2 v) {
+  const float2 av = make_float2(fabsf(v.x), fabsf(v.y));
+  float2 p = fma2(splat2(kErfC6), av, splat2(kErfC5));
+  p = fma2(p, av, splat2(kErfC4));
+  p = fma2(p, av, splat2(kErfC3));
+  p = fma2(p, av, splat2(kErfC2));
+  p = fma2(p, av, splat2(kErfC1));
+  p = fma2(p, av, splat2(1.f));
+  float2 q = make_float2(rcp_approx(p.x), rcp_approx(p.y));
+  q = mul2(q, q);
+  q = mul2(q, q);
+  q = mul2(q, q);
+  q = mul2(q, q);
+  const float2 out = fma2(mul2(av, q), splat2(-0.5f), make_float2(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f)));
+  return pack_bf16x2(out.x, out.y);
+}
+
+// Per-warp bf16 staging of a 32-row x 32-column block: row r holds 64 bytes
+// (four 16-byte chunks), chunk q stored at position q ^ ((r >> 1) & 3), so
+// that the row-per-thread 128-bit writes and the 8-rows-per-instruction
+// 128-bit reads are both free of bank conflicts.
+__device__ __forceinline__ void stage_row_bf16(uint32_t* stage, int row, const uint32_t (&w)[16]) {
+  const int sw = (row >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(stage + row * 16 + 4 * (q ^ sw)) = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
+// Writes the staged block to dst rows [row0, row0 + 32) x 32 columns (bf16),
+// 16 bytes per lane, 8 full 64-byte row segments per instruction.
+__device__ __forceinline__ void store_staged_bf16(const uint32_t* stage, int lane, __nv_bfloat16* dst, int64_t stride,
+                                                  int64_t row0, int64_t rows) {
+  const int q = lane & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int rr = 8 * j + (lane >> 2);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 16 + 4 * (q ^ ((rr >> 1) & 3)));
+    const int64_t m = row0 + rr;
+    if (m < rows) *reinterpret_cast<uint4*>(dst + m * stride + 8 * q) = val;
+  }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ float2 f2(uint32_t lo, uint32_t hi) { return make_float2(__uint_as_float(lo), __uint_as_float(hi)); }
+
+// Hands the accumulator buffer back to the MMA warp once this warp's TMEM reads are complete.
+__device__ __forceinline__ void release_acc(uint64_t* acc_empty, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(acc_empty);
+}
+
+// fp32 staging of a 32-row x 32-column block (per warp): row r holds eight
+// 16-byte chunks, chunk q stored at position q ^ (r & 7).  Row-per-thread
+// 128-bit accesses and column-per-lane 32-bit accesses are both conflict free.
+__device__ __forceinline__ int fstage_index(int row, int col) {
+  return row * 32 + 4 * ((col >> 2) ^ (row & 7)) + (col & 3);
+}
+
+// GELU epilogue of one warp: 32 rows x NT columns from TMEM (row = lane),
+// 32 columns per step; the next step's TMEM load is in flight while this one
+// computes, and the accumulator is released as soon as the last load landed.
+template <int NT>
+__device__ __forceinline__ void epilogue_gelu(uint32_t acc, const float* sbias, uint32_t* stage, int lane,
+                                              __nv_bfloat16* out, int64_t out_stride, int64_t wrow0, int64_t rows,
+                                              uint64_t* acc_empty) {
+  constexpr int kSteps = NT / 32;
+  uint32_t lo[2][16], hi[2][16];
+  tmem_ld16(acc, lo[0]);
+  tmem_ld16(acc + 16, hi[0]);
+  tmem_wait_ld();
+  reg_fence16(lo[0]);
+  reg_fence16(hi[0]);
+#pragma unroll
+  for (int s = 0; s < kSteps; ++s) {
+    const int b = s & 1;
+    if (s + 1 < kSteps) {
+      tmem_ld16(acc + 32 * (s + 1), lo[b ^ 1]);
+      tmem_ld16(acc + 32 * (s + 1) + 16, hi[b ^ 1]);
+    } else {
+      release_acc(acc_empty, lane);
+    }
+    uint32_t w[16];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // columns 32 s + 4 q .. + 3
+      const float4 bb = reinterpret_cast<const float4*>(sbias + 32 * s)[q];
+      const uint32_t* r = q < 4 ? lo[b] : hi[b];
+      const int j = 4 * (q & 3);
+      w[2 * q] = gelu_bf16x2(add2(f2(r[j], r[j + 1]), make_float2(bb.x, bb.y)));
+      w[2 * q + 1] = gelu_bf16x2(add2(f2(r[j + 2], r[j + 3]), make_float2(bb.z, bb.w)));
+    }
+    uint32_t* sb = stage + 512 * b;
+    stage_row_bf16(sb, lane, w);
+    __syncwarp();
+    store_staged_bf16(sb, lane, out + 32 * s, out_stride, wrow0, rows);
+    if (s + 1 < kSteps) {
+      tmem_wait_ld();
+      reg_fence16(lo[b ^ 1]);
+      reg_fence16(hi[b ^ 1]);
+    }
+  }
+  __syncwarp();
+}
+
+// Residual chunk copy: rows [row0, row0 + 32) x 32 fp32 columns of x into a
+// per-warp buffer in the fstage layout, 16 bytes per lane per instruction (8
+// lanes per 128-byte row segment), asynchronously (cp.async, no registers).
+// Rows past the matrix are zero-filled without reading.
+__device__ __forceinline__ void copy_x_chunk(float* buf, const float* x, int64_t x_stride, int64_t row0, int64_t rows,
+                                             int col0, int lane) {
+  const int q = lane & 7;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int r = 4 * j + (lane >> 3);
+    const bool in = row0 + r < rows;
+    const float* src = in ? x + (row0 + r) * x_stride + col0 + 4 * q : x;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(buf + fstage_index(r, 4 * q))),
+                 "l"(src), "r"(in ? 16 : 0)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Residual + LayerNorm epilogue of one warp (32 rows = lanes, NT columns):
+//   pass 1, 32 columns per step: v = C + bias + x (row per thread, x from the
+//     step's buffer); v written over x in the buffer and from there back to x
+//     in global memory (coalesced); v into TMEM; the step's row mean and sum
+//     of squared deviations merged into the running ones (Chan, Golub &
+//     LeVeque's pairwise update), so no separate variance pass;
+//   pass 2: h = bf16((v - mean) rstd gamma + beta).
+// The residual chunk of step s + 1 is copied while step s works; the caller
+// started the copy of step 0 into xbuf[0] before the accumulator was ready.
+template <int NT>
+__device__ __forceinline__ void epilogue_residual_ln(uint32_t acc, const float* sparams, float* xbuf, int lane,
+                                                     float* x, int64_t x_stride, float eps, __nv_bfloat16* h,
+                                                     int64_t h_stride, int64_t wrow0, int64_t rows,
+                                                     uint64_t* acc_empty) {
+  constexpr int kSteps = NT / 32;
+  const float* sbias = sparams;
+  const float* sgamma = sparams + NT;
+  const float* sbeta = sparams + 2 * NT;
+  float mean = 0.f, m2 = 0.f;
+#pragma unroll 1
+  for (int s = 0; s < kSteps; ++s) {
+    const int c = 32 * s;
+    float* buf = xbuf + 1024 * (s & 1);
+    if (s + 1 < kSteps) copy_x_chunk(xbuf + 1024 * ((s + 1) & 1), x, x_stride, wrow0, rows, c + 32, lane);
+    uint32_t lo[16], hi[16];
+    tmem_ld16(acc + c, lo);
+    tmem_ld16(acc + c + 16, hi);
+    if (s + 1 < kSteps)
+      cp_async_wait<1>();
+    else
+      cp_async_wait<0>();
+    __syncwarp();
+    tmem_wait_ld();
+    reg_fence16(lo);
+    reg_fence16(hi);
+    float2 p[16];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4* cell = reinterpret_cast<float4*>(buf + fstage_index(lane, 4 * q));
+      const float4 xv = *cell;
+      const float4 bb = reinterpret_cast<const float4*>(sbias + c)[q];
+      const uint32_t* r = q < 4 ? lo : hi;
+      const int j = 4 * (q & 3);
+      p[2 * q] = add2(add2(f2(r[j], r[j + 1]), make_float2(bb.x, bb.y)), make_float2(xv.x, xv.y));
+      p[2 * q + 1] = add2(add2(f2(r[j + 2], r[j + 3]), make_float2(bb.z, bb.w)), make_float2(xv.z, xv.w));
+      *cell = make_float4(p[2 * q].x, p[2 * q].y, p[2 * q + 1].x, p[2 * q + 1].y);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      lo[2 * k] = __float_as_uint(p[k].x);
+      lo[2 * k + 1] = __float_as_uint(p[k].y);
+      hi[2 * k] = __float_as_uint(p[8 + k].x);
+      hi[2 * k + 1] = __float_as_uint(p[8 + k].y);
+    }
+    tmem_st16(acc + c, lo);
+    tmem_st16(acc + c + 16, hi);
+    __syncwarp();
+    {  // v back to the residual stream: 4 rows x 128 bytes per instruction
+      const int q = lane & 7;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = 4 * j + (lane >> 3);
+        const float4 v = *reinterpret_cast<const float4*>(buf + fstage_index(r, 4 * q));
+        if (wrow0 + r < rows) *reinterpret_cast<float4*>(x + (wrow0 + r) * x_stride + c + 4 * q) = v;
+      }
+    }
+    // step statistics: pairwise sums, then the squared deviations about the step mean
+    float2 t4[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) t4[k] = add2(add2(p[4 * k], p[4 * k + 1]), add2(p[4 * k + 2], p[4 * k + 3]));
+    const float2 t2 = add2(add2(t4[0], t4[1]), add2(t4[2], t4[3]));
+    const float mb = (t2.x + t2.y) * (1.f / 32.f);
+    float2 d4[4] = {splat2(0.f), splat2(0.f), splat2(0.f), splat2(0.f)};
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float2 d = add2(p[k], splat2(-mb));
+      d4[k & 3] = fma2(d, d, d4[k & 3]);
+    }
+    const float2 dd = add2(add2(d4[0], d4[1]), add2(d4[2], d4[3]));
+    const float m2b = dd.x + dd.y;
+    if (s == 0) {
+      mean = mb;
+      m2 = m2b;
+    } else {
+      const float delta = mb - mean;
+      mean = fmaf(delta, 32.f / (c + 32), mean);
+      m2 += fmaf(delta * delta, (32.f * c) / (c + 32), m2b);
+    }
+    __syncwarp();
+  }
+  tmem_wait_st();
+  const float rstd = rsqrtf(m2 * (1.f / NT) + eps);
+  const float2 neg_mean = splat2(-mean), rstd2 = splat2(rstd);
+  uint32_t* stage = reinterpret_cast<uint32_t*>(xbuf);
+  uint32_t lo[2][16], hi[2][16];
+  tmem_ld16(acc, lo[0]);
+  tmem_ld16(acc + 16, hi[0]);
+  tmem_wait_ld();
+  reg_fence16(lo[0]);
+  reg_fence16(hi[0]);
+#pragma unroll
+  for (int s = 0; s < kSteps; ++s) {
+    const int c = 32 * s, b = s & 1;
+    if (s + 1 < kSteps) {
+      tmem_ld16(acc + c + 32, lo[b ^ 1]);
+      tmem_ld16(acc + c + 48, hi[b ^ 1]);
+    } else {
+      release_acc(acc_empty, lane);
+    }
+    uint32_t w[16];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // columns c + 4 q .. + 3
+      const float4 ga = reinterpret_cast<const float4*>(sgamma + c)[q];
+      const float4 be = reinterpret_cast<const float4*>(sbeta + c)[q];
+      const uint32_t* r = q < 4 ? lo[b] : hi[b];
+      const int j = 4 * (q & 3);
+      const float2 d0 = mul2(add2(f2(r[j], r[j + 1]), neg_mean), rstd2);
+      const float2 d1 = mul2(add2(f2(r[j + 2], r[j + 3]), neg_mean), rstd2);
+      const float2 o0 = fma2(d0, make_float2(ga.x, ga.y), make_float2(be.x, be.y));
+      const float2 o1 = fma2(d1, make_float2(ga.z, ga.w), make_float2(be.z, be.w));
+      w[2 * q] = pack_bf16x2(o0.x, o0.y);
+      w[2 * q + 1] = pack_bf16x2(o1.x, o1.y);
+    }
+    uint32_t* sb = stage + 512 * b;
+    stage_row_bf16(sb, lane, w);
+    __syncwarp();
+    store_staged_bf16(sb, lane, h + c, h_stride, wrow0, rows);
+    if (s + 1 < kSteps) {
+      tmem_wait_ld();
+      reg_fence16(lo[b ^ 1]);
+      reg_fence16(hi[b ^ 1]);
+    }
+  }
+  __syncwarp();
+}
 
 template <int NT, int STAGES, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const GemmArgs g) {
   constexpr uint32_t kBSlab = NT * kGBK * 2;
@@ -83,7 +382,7 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
-      mbar_init(&bars->acc_empty[b], 4);
+      mbar_init(&bars->acc_empty[b], 4 * epi_groups_per_tile<EPI>());
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -92,6 +391,17 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
+  }
+  // epilogue parameters in shared memory: GELU bias (N), or LN bias | gamma | beta (NT each)
+  float* sparams = reinterpret_cast<float*>(smem + STAGES * kStage + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4);
+  if (EPI == kEpiGelu) {
+    for (int i = threadIdx.x; i < g.N; i += gemm_threads<EPI>()) sparams[i] = g.bias[i];
+  } else {
+    for (int i = threadIdx.x; i < NT; i += gemm_threads<EPI>()) {
+      sparams[i] = g.bias[i];
+      sparams[NT + i] = g.gamma[i];
+      sparams[2 * NT + i] = g.beta[i];
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -175,143 +485,45 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
         mbar_wait(&bars->drain, 0, &no_abort, g.status, kDevTimeoutDrain);
       }
     }
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------ epilogue warpgroups
-    const uint32_t e = (warp - 4) >> 2;   // warpgroup: takes local tiles with lt % 2 == e
+    constexpr int kSplit = epi_groups_per_tile<EPI>();
+    constexpr int kCols = NT / kSplit;                      // columns per group
+    const int grp = (warp - 2) >> 2;
+    const uint32_t e = grp / kSplit;                        // takes local tiles with lt % 2 == e
+    const int col0 = (grp % kSplit) * kCols;                // first tile column of this group
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + STAGES * kStage + kBarrierBytes) + (warp - 4) * kStageWords;
+    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + STAGES * kStage + kBarrierBytes) + (warp - 2) * stage_words<EPI>();
     uint32_t lt = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++lt) {
       if ((lt & 1) != e) continue;
-      if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
       const int32_t n0 = static_cast<int32_t>((t % g.n_tiles_n) * NT);
-      const uint32_t acc = lane_base + e * NT;
-      // Warp-cooperative global traffic: a chunk of 32 columns of the warp's 32
-      // rows is staged in `stage` (row pitch 33 words: conflict free both ways)
-      // and moved one row per instruction, 32 lanes on 32 consecutive columns.
+      const uint32_t acc = lane_base + e * NT + col0;
       const int64_t wrow0 = (t / g.n_tiles_n) * kGBM + (warp & 3) * 32;  // first row of this warp
       if (EPI == kEpiGelu) {
-#pragma unroll 1
-        for (int c = 0; c < NT; c += 32) {
-          uint32_t r0[16], r1[16];
-          tmem_ld16(acc + c, r0);
-          tmem_ld16(acc + c + 16, r1);
-          tmem_wait_ld();
-          reg_fence16(r0);
-          reg_fence16(r1);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int n = n0 + c + 2 * i;
-            stage[lane * 33 + i] = pack_bf16x2(gelu_erf(__uint_as_float(r0[2 * i]) + __ldg(g.bias + n)),
-                                               gelu_erf(__uint_as_float(r0[2 * i + 1]) + __ldg(g.bias + n + 1)));
-            stage[lane * 33 + 8 + i] =
-                pack_bf16x2(gelu_erf(__uint_as_float(r1[2 * i]) + __ldg(g.bias + n + 16)),
-                            gelu_erf(__uint_as_float(r1[2 * i + 1]) + __ldg(g.bias + n + 17)));
-          }
-          __syncwarp();
-          // 16 words (32 bf16) per row: lanes 0-15 row i, lanes 16-31 row i + 1
-#pragma unroll 4
-          for (int i = 0; i < 32; i += 2) {
-            const int rr = i + (lane >> 4);
-            const int64_t m = wrow0 + rr;
-            if (m < g.M)
-              reinterpret_cast<uint32_t*>(g.out + m * g.out_stride + n0 + c)[lane & 15] = stage[rr * 33 + (lane & 15)];
-          }
-          __syncwarp();
+        if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        epilogue_gelu<kCols>(acc, sparams + n0 + col0, stage, lane, g.out + n0 + col0, g.out_stride, wrow0, g.M,
+                             &bars->acc_empty[e]);
       } else {
-        // pass 1: v = C + bias + x; x written back; v kept in TMEM; row sum
-        float sum = 0.f;
-        float* fstage = reinterpret_cast<float*>(stage);
-#pragma unroll 1
-        for (int c = 0; c < NT; c += 32) {
-          uint32_t r0[16], r1[16];
-          tmem_ld16(acc + c, r0);
-          tmem_ld16(acc + c + 16, r1);
-          tmem_wait_ld();
-          reg_fence16(r0);
-          reg_fence16(r1);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            fstage[lane * 33 + i] = __uint_as_float(r0[i]) + __ldg(g.bias + c + i);
-            fstage[lane * 33 + 16 + i] = __uint_as_float(r1[i]) + __ldg(g.bias + c + 16 + i);
-          }
-          __syncwarp();
-#pragma unroll 4
-          for (int i = 0; i < 32; ++i) {
-            const int64_t m = wrow0 + i;
-            if (m < g.M) {
-              float* xp = g.x + m * g.x_stride + c + lane;
-              const float v = fstage[i * 33 + lane] + *xp;
-              *xp = v;
-              fstage[i * 33 + lane] = v;
-            }
-          }
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            r0[i] = __float_as_uint(fstage[lane * 33 + i]);
-            r1[i] = __float_as_uint(fstage[lane * 33 + 16 + i]);
-            sum += __uint_as_float(r0[i]) + __uint_as_float(r1[i]);
-          }
-          __syncwarp();
-          tmem_st16(acc + c, r0);
-          tmem_st16(acc + c + 16, r1);
+        // The residual rows are fetched into L2, and their first 32 columns
+        // into shared memory, while the tile still accumulates.
+        float* xbuf = reinterpret_cast<float*>(stage);
+        if (wrow0 + lane < g.M) prefetch_l2(g.x + (wrow0 + lane) * g.x_stride, NT * 4);
+        copy_x_chunk(xbuf, g.x, g.x_stride, wrow0, g.M, 0, lane);
+        if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
+          cp_async_wait<0>();
+          ok = false;
+          break;
         }
-        tmem_wait_st();
-        const float mean = sum * (1.f / NT);
-        // pass 2: variance about the mean
-        float var = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < NT; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(acc + c, r);
-          tmem_wait_ld();
-          reg_fence16(r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float d = __uint_as_float(r[i]) - mean;
-            var = fmaf(d, d, var);
-          }
-        }
-        const float rstd = rsqrtf(var * (1.f / NT) + g.eps);
-        // pass 3: h = bf16((v - mean) * rstd * gamma + beta), staged like the GELU output
-#pragma unroll 1
-        for (int c = 0; c < NT; c += 32) {
-          uint32_t r0[16], r1[16];
-          tmem_ld16(acc + c, r0);
-          tmem_ld16(acc + c + 16, r1);
-          tmem_wait_ld();
-          reg_fence16(r0);
-          reg_fence16(r1);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int n = c + 2 * i;
-            stage[lane * 33 + i] = pack_bf16x2(
-                fmaf((__uint_as_float(r0[2 * i]) - mean) * rstd, __ldg(g.gamma + n), __ldg(g.beta + n)),
-                fmaf((__uint_as_float(r0[2 * i + 1]) - mean) * rstd, __ldg(g.gamma + n + 1), __ldg(g.beta + n + 1)));
-            stage[lane * 33 + 8 + i] = pack_bf16x2(
-                fmaf((__uint_as_float(r1[2 * i]) - mean) * rstd, __ldg(g.gamma + n + 16), __ldg(g.beta + n + 16)),
-                fmaf((__uint_as_float(r1[2 * i + 1]) - mean) * rstd, __ldg(g.gamma + n + 17), __ldg(g.beta + n + 17)));
-          }
-          __syncwarp();
-#pragma unroll 4
-          for (int i = 0; i < 32; i += 2) {
-            const int rr = i + (lane >> 4);
-            const int64_t m = wrow0 + rr;
-            if (m < g.M) reinterpret_cast<uint32_t*>(g.h + m * g.h_stride + c)[lane & 15] = stage[rr * 33 + (lane & 15)];
-          }
-          __syncwarp();
-        }
+        tc_fence_after();
+        epilogue_residual_ln<NT>(acc, sparams, xbuf, lane, g.x, g.x_stride, g.eps, g.h, g.h_stride, wrow0, g.M,
+                                 &bars->acc_empty[e]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->acc_empty[e]);
     }
   }
 
@@ -354,12 +566,13 @@ intp_status launch_gemm(const void* a, int64_t a_stride, const void* w, GemmArgs
     return INTP_ERR_LAUNCH;
   auto kernel = gemm_epilogue_kernel<NT, STAGES, EPI>;
   static_assert(sizeof(GemmBarriers<STAGES>) <= kBarrierBytes, "barrier block");
-  const size_t smem = 1024 + STAGES * (kASlab + NT * kGBK * 2) + kBarrierBytes + 8 * kStageWords * 4;
+  const size_t params = EPI == kEpiGelu ? static_cast<size_t>(g.N) : 3 * NT;
+  const size_t smem = 1024 + STAGES * (kASlab + NT * kGBK * 2) + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4 + params * 4;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return INTP_ERR_LAUNCH;
   const int64_t grid = g.tiles < sms ? g.tiles : sms;
-  kernel<<<static_cast<unsigned>(grid), kGemmThreads, smem, stream>>>(ma, mb, g);
+  kernel<<<static_cast<unsigned>(grid), gemm_threads<EPI>(), smem, stream>>>(ma, mb, g);
   return cudaGetLastError() == cudaSuccess ? INTP_OK : INTP_ERR_LAUNCH;
 }
 
@@ -379,8 +592,9 @@ extern "C" INTP_API intp_status svit_linear_gelu(const void* a, int64_t a_stride
                                                  void* out, int64_t out_stride, int32_t* status, void* stream) {
   if (rows < 0 || in_features < 1 || out_features < 1) return INTP_ERR_SHAPE;
   if (rows == 0) return INTP_OK;
+  if (out_features > kMaxGeluN) return INTP_ERR_UNSUPPORTED;
   if (!a || !weight || !bias || !out || !status) return INTP_ERR_ARGUMENT;
-  if (a_stride < in_features || out_stride < out_features || out_stride % 8 || !aligned16(out))
+  if (a_stride < in_features || out_stride < out_features || out_stride % 8 || !aligned16(out) || !aligned16(bias))
     return INTP_ERR_LAYOUT;
   if (!device_is_sm100()) return INTP_ERR_ARCH;
   GemmArgs g{};
@@ -405,7 +619,7 @@ extern "C" INTP_API intp_status svit_linear_residual_layernorm(const void* a, in
   if (!a || !weight || !bias || !x || !gamma || !beta || !h || !status) return INTP_ERR_ARGUMENT;
   if (dim != 192) return INTP_ERR_UNSUPPORTED;
   if (a_stride < in_features || x_stride < dim || h_stride < dim || x_stride % 4 || h_stride % 8 || !aligned16(x) ||
-      !aligned16(h))
+      !aligned16(h) || !aligned16(bias) || !aligned16(gamma) || !aligned16(beta))
     return INTP_ERR_LAYOUT;
   if (!device_is_sm100()) return INTP_ERR_ARCH;
   GemmArgs g{};
@@ -421,5 +635,5 @@ extern "C" INTP_API intp_status svit_linear_residual_layernorm(const void* a, in
   g.h = static_cast<__nv_bfloat16*>(h);
   g.h_stride = h_stride;
   g.status = status;
-  return launch_gemm<192, 4, kEpiResidualLN>(a, a_stride, weight, g, static_cast<cudaStream_t>(stream));
+  return launch_gemm<192, 3, kEpiResidualLN>(a, a_stride, weight, g, static_cast<cudaStream_t>(stream));
 }
