@@ -49,10 +49,19 @@ typedef int32_t intp_status;
  * SLOTS   : the same bias when fields[h,p,q,k] is the one-hot indicator of a
  *           per-pair slot index: bias[b,h,i,j] = pose[b,i-1,h,slot(i,j)]
  *           (zero where the pair has no slot).  The pair table is prepared
- *           once by sla_pack_slot_table and shared by every batch and head.  */
-#define SLA_BIAS_NONE    0
-#define SLA_BIAS_FIELDS  1
-#define SLA_BIAS_SLOTS   2
+ *           once by sla_pack_slot_table and shared by every batch and head.
+ * SLOT_FIELDS : FIELDS when each field is a per-slot value gathered by the same
+ *           pair table: fields[h,p,i-1,j-1] = slot_fields[h,p,slot(i,j)], so
+ *           bias[b,h,i,j] = sum_p pose[b,i-1,h,p] * slot_fields[h,p,slot(i,j)]
+ *           (zero where the pair has no slot).  This is the reference model's
+ *           Look-bank call (model/deit_tiny_rot_hex_look.py:397-451 ->
+ *           layers/mini_vit.py:103) with its (H, P, Np, Np) fields held as
+ *           (H, P, S) slot values: `fields` = slot_fields, `poses` = P,
+ *           `slots` = S.                                                    */
+#define SLA_BIAS_NONE         0
+#define SLA_BIAS_FIELDS       1
+#define SLA_BIAS_SLOTS        2
+#define SLA_BIAS_SLOT_FIELDS  3
 
 /* Slot value meaning "no Look bias for this pair" in an unpacked slot table. */
 #define SLA_SLOT_NONE 255
@@ -67,11 +76,13 @@ typedef int32_t intp_status;
  * Tensors follow the reference layouts (layers/triton_structured_look_attention.py:412-424):
  *   q, k, v, out : (B, H, N, D), N = Np + 1 (token 0 is CLS), any strides, D stride 1
  *   pose         : (B, Np, H, P) floating, any strides
- *   fields       : (H, P, Np, Np) floating (FIELDS mode only), any strides
+ *   fields       : (H, P, Np, Np) floating (FIELDS mode), any strides;
+ *                  (H, P, S) slot_fields (SLOT_FIELDS mode), strides [0..2]
  *   dense        : (B, H, Np, Np) floating or NULL, any strides
  *   lse          : (B, H, N) float32 contiguous, or NULL when not wanted
- * Strides are in elements.  In SLOTS mode `slots_packed` / `slot_tile_flags`
- * come from sla_pack_slot_table for this N and are device pointers.          */
+ * Strides are in elements.  In SLOTS and SLOT_FIELDS modes `slots_packed` /
+ * `slot_tile_flags` come from sla_pack_slot_table for this N and are device
+ * pointers.                                                                 */
 typedef struct sla_forward_args {
   int64_t batch, heads, seq, head_dim;
   float scale;
@@ -82,7 +93,7 @@ typedef struct sla_forward_args {
   void* out;     int64_t out_stride[4];
   float* lse;
   int32_t bias_mode;
-  int64_t poses;                 /* P (FIELDS) or number of slots (SLOTS)     */
+  int64_t poses;                 /* P (FIELDS, SLOT_FIELDS) or slots (SLOTS)  */
   const void* pose;   int64_t pose_stride[4];   int32_t pose_dtype;
   const void* fields; int64_t fields_stride[4]; int32_t fields_dtype;
   const uint8_t* slots_packed;
@@ -90,6 +101,7 @@ typedef struct sla_forward_args {
   const void* dense;  int64_t dense_stride[4];  int32_t dense_dtype;
   int32_t* status;               /* device int32: bounded-wait error word     */
   int32_t kernel;                /* SLA_KERNEL_*                              */
+  int64_t slots;                 /* S, number of slots (SLOT_FIELDS mode)     */
 } sla_forward_args;
 
 /* Structured Look attention forward.

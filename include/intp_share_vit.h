@@ -64,7 +64,12 @@ typedef struct svit_embed_args {
   float* x;                     /* out: (batch, patches + 1, 2*bases) tokens     */
   float* values;                /* out: (batch, look_heads, patches, slots):     */
                                 /* per image and head, the patches' slot values  */
-                                /* are contiguous                                */
+                                /* are contiguous.  May be NULL (see look_pose)  */
+  float* look_pose;             /* out (optional): (batch, patches, look_heads,  */
+                                /* look_poses) Look pose after the null softmax; */
+                                /* with values NULL only x and look_pose are     */
+                                /* written (the attention forms the per-slot     */
+                                /* values itself, SLA_BIAS_SLOT_FIELDS)          */
 } svit_embed_args;
 
 INTP_API intp_status svit_embed_post(const svit_embed_args* args, void* stream);

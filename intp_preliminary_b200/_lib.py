@@ -24,8 +24,9 @@ INTP_ERR_TIMEOUT = 7
 INTP_ERR_UNSUPPORTED = 8
 
 INTP_F32, INTP_F16, INTP_BF16 = 0, 1, 2
-SLA_BIAS_NONE, SLA_BIAS_FIELDS, SLA_BIAS_SLOTS = 0, 1, 2
+SLA_BIAS_NONE, SLA_BIAS_FIELDS, SLA_BIAS_SLOTS, SLA_BIAS_SLOT_FIELDS = 0, 1, 2, 3
 SLA_SLOT_NONE = 255
+ABI_VERSION = 2
 SLA_KERNEL_AUTO, SLA_KERNEL_SIMT, SLA_KERNEL_TCGEN05 = 0, 1, 2
 
 # Every symbol include/intp_b200.h declares.
@@ -78,6 +79,7 @@ class SlaForwardArgs(ctypes.Structure):
         ("dense", _vp), ("dense_stride", _Stride), ("dense_dtype", _i32),
         ("status", _vp),
         ("kernel", _i32),
+        ("slots", _i64),
     ]
 
 
@@ -107,6 +109,7 @@ class SvitEmbedArgs(ctypes.Structure):
         ("token_null", _vp), ("direction_coef", _vp), ("output_bias", _vp),
         ("cls", _vp), ("pos_embed", _vp), ("look_null", _vp), ("slot_fields", _vp),
         ("x", _vp), ("values", _vp),
+        ("look_pose", _vp),
     ]
 
 
@@ -165,7 +168,7 @@ def load() -> ctypes.CDLL:
         lib.intp_abi_version.restype = _i32
         lib.intp_status_string.argtypes = [_i32]
         lib.intp_status_string.restype = ctypes.c_char_p
-        if lib.intp_abi_version() != 1:
+        if lib.intp_abi_version() != ABI_VERSION:
             raise NativeLibraryError("libintp_b200.so ABI version mismatch")
         _lib = lib
         return lib

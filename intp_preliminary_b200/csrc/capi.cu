@@ -46,7 +46,7 @@ bool valid_dtype(int32_t d) { return d == INTP_F32 || d == INTP_F16 || d == INTP
 
 extern "C" {
 
-int32_t intp_abi_version(void) { return 1; }
+int32_t intp_abi_version(void) { return 2; }
 
 const char* intp_status_string(intp_status s) {
   switch (s) {
@@ -148,6 +148,11 @@ intp_status to_params(const sla_forward_args* a, intp::SlaParams* out, bool* emp
     if (!a->pose || !a->slots_packed || !a->slot_tile_flags || a->poses < 1 || a->poses > 253)
       return INTP_ERR_ARGUMENT;
     if (!valid_dtype(a->pose_dtype)) return INTP_ERR_DTYPE;
+  } else if (a->bias_mode == SLA_BIAS_SLOT_FIELDS) {
+    if (!a->pose || !a->fields || !a->slots_packed || !a->slot_tile_flags || a->poses < 1 || a->slots < 1 ||
+        a->slots > 253)
+      return INTP_ERR_ARGUMENT;
+    if (!valid_dtype(a->pose_dtype) || !valid_dtype(a->fields_dtype)) return INTP_ERR_DTYPE;
   } else if (a->bias_mode != SLA_BIAS_NONE) {
     return INTP_ERR_ARGUMENT;
   }
@@ -173,6 +178,7 @@ intp_status to_params(const sla_forward_args* a, intp::SlaParams* out, bool* emp
   p.lse = a->lse;
   p.bias_mode = a->bias_mode;
   p.poses = a->poses;
+  p.slots = a->bias_mode == SLA_BIAS_SLOT_FIELDS ? a->slots : 0;
   p.pose = a->pose;
   std::memcpy(p.pose_stride, a->pose_stride, sizeof(p.pose_stride));
   p.pose_dtype = a->pose_dtype;
@@ -214,6 +220,9 @@ intp_status sla_backward(const sla_backward_args* a, void* stream) {
   const intp_status st = to_params(&a->fwd, &bp.f, &empty);
   if (st != INTP_OK || empty) return st;
   if (!a->fwd.lse || !a->grad_out || !a->delta) return INTP_ERR_ARGUMENT;
+  // SLOT_FIELDS gradients go through the SLOTS form with the per-slot values
+  // pose . slot_fields materialised by the caller.
+  if (a->fwd.bias_mode == SLA_BIAS_SLOT_FIELDS) return INTP_ERR_UNSUPPORTED;
   if (a->grad_fields && a->fwd.bias_mode != SLA_BIAS_FIELDS) return INTP_ERR_ARGUMENT;
   if (a->grad_pose && a->fwd.bias_mode == SLA_BIAS_NONE) return INTP_ERR_ARGUMENT;
   if (a->grad_dense && !a->fwd.dense) return INTP_ERR_ARGUMENT;

@@ -137,10 +137,6 @@ __device__ __forceinline__ void store_staged_bf16(const uint32_t* stage, int lan
   }
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ float2 f2(uint32_t lo, uint32_t hi) { return make_float2(__uint_as_float(lo), __uint_as_float(hi)); }
 
 // Hands the accumulator buffer back to the MMA warp once this warp's TMEM reads are complete.
@@ -513,7 +509,7 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
         // The residual rows are fetched into L2, and their first 32 columns
         // into shared memory, while the tile still accumulates.
         float* xbuf = reinterpret_cast<float*>(stage);
-        if (wrow0 + lane < g.M) prefetch_l2(g.x + (wrow0 + lane) * g.x_stride, NT * 4);
+        if (wrow0 + lane < g.M) bulk_prefetch_l2(g.x + (wrow0 + lane) * g.x_stride, NT * 4);
         copy_x_chunk(xbuf, g.x, g.x_stride, wrow0, g.M, 0, lane);
         if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
           cp_async_wait<0>();

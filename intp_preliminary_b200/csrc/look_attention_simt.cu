@@ -1,7 +1,7 @@
 // look_attention_simt.cu - CUDA-core structured Look attention forward.
 //
 // This is the coverage path: every dtype (f32/f16/bf16), any head_dim <= 128,
-// any strides, all three bias modes (none / general fields / slots) and the
+// any strides, every bias mode (none / general fields / slots / slot fields) and the
 // optional dense bias.  It computes exactly the reference semantics
 // (layers/triton_structured_look_attention.py:25-54):
 //   S = scale * q k^T (fp32);  S[1:,1:] += sum_p pose * fields  (+ dense);
@@ -125,6 +125,21 @@ sla_simt_kernel(const SlaParams p) {
             bias = load_any(p.pose, b * p.pose_stride[0] + pq * p.pose_stride[1] + h * p.pose_stride[2] +
                                         slot * p.pose_stride[3],
                             p.pose_dtype);
+        } else if (p.bias_mode == 3) {
+          const int64_t qt = i >> 7, kt = kj >> 6;
+          const int64_t off = (qt * n_kt64 + kt) * 8192 + ((kj & 63) >> 4) * 2048 + (i & 127) * 16 + (kj & 15);
+          const int slot = p.slots_packed[off];
+          if (slot < p.slots) {
+            for (int64_t pp = 0; pp < p.poses; ++pp) {
+              const float w = load_any(p.pose, b * p.pose_stride[0] + pq * p.pose_stride[1] +
+                                                   h * p.pose_stride[2] + pp * p.pose_stride[3],
+                                       p.pose_dtype);
+              const float f = load_any(p.fields, h * p.fields_stride[0] + pp * p.fields_stride[1] +
+                                                     slot * p.fields_stride[2],
+                                       p.fields_dtype);
+              bias = fmaf(w, f, bias);
+            }
+          }
         }
         if (p.dense != nullptr)
           bias += load_any(p.dense, b * p.dense_stride[0] + h * p.dense_stride[1] + pq * p.dense_stride[2] +

@@ -3,7 +3,11 @@
 // Semantics: layers/triton_structured_look_attention.py:25-54 (oracle) and
 // :57-169 (the reference's Triton forward), for bf16 / f16 inputs, head_dim 64,
 // with the Look bias in SLOTS form (bias[b,h,i,j] = pose[b,i-1,h,slot(i,j)],
-// the one-hot-fields case of the reference API) or no bias.
+// the one-hot-fields case of the reference API), in SLOT_FIELDS form
+// (bias = sum_p pose[b,i-1,h,p] * slot_fields[h,p,slot(i,j)]: the reference
+// model's fields, stored per slot) or without bias.  Either Look form becomes
+// a per-query table of slot values in shared memory at the start of a work
+// item; the score tiles then gather from it by the packed pair table.
 //
 // CTA organisation (192 threads, two CTAs per SM):
 //   warps 0-3  softmax warpgroup: thread t owns query row t of the 128-row tile.
@@ -54,6 +58,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 2^8
 constexpr int kMaxSlots = 93;
+constexpr int kMaxPoses = 16;      // SLOT_FIELDS: Look poses per head
 template <int KS>
 struct alignas(8) Barriers {
   uint64_t q_full, q_empty;
@@ -63,6 +68,8 @@ struct alignas(8) Barriers {
   // pv_done[b]: the PV that read that P finished (buffer b is free again).
   // One barrier per buffer keeps every waiter at most one phase behind.
   uint64_t s_full[2], p_full[2], pv_done[2];
+  uint64_t sf_ready;  // SLOT_FIELDS: an item's slot values are staged (4 softmax warps)
+  uint64_t sf_free;   // SLOT_FIELDS: the 4 softmax warps built that item's table
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
@@ -144,7 +151,13 @@ struct TcArgs {
   int64_t n_qt, n_kt, n_items;
   int32_t n_slots;        // 0 when there is no Look bias
   uint32_t table_bytes;   // bytes of the per-query Look table in smem
-  int32_t pose_vec4;      // pose rows are 16-byte aligned fp32 with unit slot stride
+  int32_t pose_vec4;      // pose rows are 16-byte aligned fp32 with unit stride along slots
+                          // (SLOTS) or poses (SLOT_FIELDS, poses % 4 == 0)
+  int32_t slot_fields;    // 1: SLOT_FIELDS mode (table = pose . slot_fields)
+  int32_t n_poses;        // SLOT_FIELDS: poses per head
+  int32_t sf_vec4;        // SLOT_FIELDS: slot_fields rows are 16-byte aligned fp32, unit slot stride;
+                          // the head's rows are then staged in smem after the table
+  uint32_t sf_offset;     // SLOT_FIELDS with sf_vec4: floats from the table start to the staged rows
 };
 
 // Per-query Look values of query token i into column `row` of the [slot][row]
@@ -158,22 +171,22 @@ __device__ __forceinline__ void stage_table(float* table_s, const TcArgs& a, int
   const bool valid = i >= 1 && i < p.seq;
   const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
   if (a.pose_vec4) {
-    // Eight 16-byte loads in flight per batch: one memory round trip per 32 slots.
+    // The whole row's 16-byte loads in flight at once: one memory round trip
+    // (an L2 hit when the previous item prefetched it).
+    constexpr int kMaxVec = kMaxSlots / 4;
     const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
-    for (int s0 = 0; s0 < ns / 4; s0 += 8) {
-      float4 v4[8];
+    float4 v4[kMaxVec];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        v4[u] = (valid && s0 + u < ns / 4) ? __ldg(src + s0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < kMaxVec; ++u)
+      v4[u] = (valid && u < ns / 4) ? __ldg(src + u) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (s0 + u < ns / 4) {
-          float* dst = table_s + 4 * (s0 + u) * BM + row;
-          dst[0] = v4[u].x * kLog2e;
-          dst[BM] = v4[u].y * kLog2e;
-          dst[2 * BM] = v4[u].z * kLog2e;
-          dst[3 * BM] = v4[u].w * kLog2e;
-        }
+    for (int u = 0; u < kMaxVec; ++u) {
+      if (u < ns / 4) {
+        float* dst = table_s + 4 * u * BM + row;
+        dst[0] = v4[u].x * kLog2e;
+        dst[BM] = v4[u].y * kLog2e;
+        dst[2 * BM] = v4[u].z * kLog2e;
+        dst[3 * BM] = v4[u].w * kLog2e;
       }
     }
   } else {
@@ -182,6 +195,137 @@ __device__ __forceinline__ void stage_table(float* table_s, const TcArgs& a, int
   }
   table_s[ns * BM + row] = 0.f;               // "no bias"
   table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
+}
+
+// SLOT_FIELDS with sf_vec4: the 128 softmax threads copy head h's slot values
+// (P rows of S fp32) into shared memory after the table; each warp then
+// arrives on sf_ready.  The copy of item k + 1 cannot overwrite rows another
+// warp still reads for item k: a warp reaches item k + 1 only after every
+// warp published all P tiles of item k, i.e. finished its table of item k.
+__device__ __forceinline__ void stage_slot_fields(float* table_s, const TcArgs& a, int64_t h, int tid) {
+  const SlaParams& p = a.p;
+  const int groups = a.n_slots / 4, total = a.n_poses * groups;
+  const float* src = static_cast<const float*>(p.fields) + h * p.fields_stride[0];
+  float4* dst = reinterpret_cast<float4*>(table_s + a.sf_offset);
+  for (int idx = tid; idx < total; idx += BM) {
+    const int pp = idx / groups, s4 = idx - pp * groups;
+    dst[idx] = __ldg(reinterpret_cast<const float4*>(src + pp * p.fields_stride[1]) + s4);
+  }
+}
+
+// SLOT_FIELDS: query token i's Look pose row (raw values; rows past the
+// sequence and the CLS token read as 0).  Issued before the slot values are
+// staged so that the two memory round trips overlap.
+__device__ __forceinline__ void load_pose_row(float (&w)[kMaxPoses], const TcArgs& a, int64_t b, int64_t h,
+                                              int64_t i) {
+  const SlaParams& p = a.p;
+  const int32_t np = a.n_poses;
+  const bool valid = i >= 1 && i < p.seq;
+  const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
+  if (a.pose_vec4) {
+    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
+#pragma unroll
+    for (int c = 0; c < kMaxPoses / 4; ++c) {
+      const float4 v = (valid && 4 * c < np) ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      w[4 * c] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+  } else if (p.pose_dtype == 0) {
+    const float* src = static_cast<const float*>(p.pose);
+#pragma unroll
+    for (int pp = 0; pp < kMaxPoses; ++pp)
+      w[pp] = (valid && pp < np) ? __ldg(src + base + pp * p.pose_stride[3]) : 0.f;
+  } else {
+#pragma unroll
+    for (int pp = 0; pp < kMaxPoses; ++pp)
+      w[pp] = (valid && pp < np) ? load_any(p.pose, base + pp * p.pose_stride[3], p.pose_dtype) : 0.f;
+  }
+}
+
+// SLOT_FIELDS: the per-query table built from the query's Look pose and the
+// head's slot fields, table[s][row] = log2(e) sum_p pose[b,i-1,h,p]
+// slot_fields[h,p,s] (model/deit_tiny_rot_hex_look.py:397-451 feeds exactly
+// this product to the attention as pose x fields).  With sf_vec4 the slot
+// values come from shared memory (stage_slot_fields; every thread reads the
+// same address), four 4-slot groups at a time so that eight accumulator
+// chains are in flight.
+__device__ __forceinline__ void build_table_sf(float* table_s, const TcArgs& a, int64_t h, int row,
+                                               float (&w)[kMaxPoses]) {
+  const SlaParams& p = a.p;
+  const int32_t ns = a.n_slots, np = a.n_poses;
+#pragma unroll
+  for (int pp = 0; pp < kMaxPoses; ++pp) w[pp] *= kLog2e;
+  if (a.sf_vec4) {
+    const float4* sf = reinterpret_cast<const float4*>(table_s + a.sf_offset);
+    const int groups = ns / 4;
+    int s4 = 0;
+    for (; s4 + 4 <= groups; s4 += 4) {
+      float2 acc[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int pp = 0; pp < kMaxPoses; ++pp) {
+        if (pp < np) {
+          const float2 wp = make_float2(w[pp], w[pp]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 f = sf[pp * groups + s4 + u];
+            acc[2 * u] = fma2(wp, make_float2(f.x, f.y), acc[2 * u]);
+            acc[2 * u + 1] = fma2(wp, make_float2(f.z, f.w), acc[2 * u + 1]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float* dst = table_s + 4 * (s4 + u) * BM + row;
+        dst[0] = acc[2 * u].x;
+        dst[BM] = acc[2 * u].y;
+        dst[2 * BM] = acc[2 * u + 1].x;
+        dst[3 * BM] = acc[2 * u + 1].y;
+      }
+    }
+    for (; s4 < groups; ++s4) {
+      float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int pp = 0; pp < kMaxPoses; ++pp) {
+        if (pp < np) {
+          const float4 f = sf[pp * groups + s4];
+          lo = fma2(make_float2(w[pp], w[pp]), make_float2(f.x, f.y), lo);
+          hi = fma2(make_float2(w[pp], w[pp]), make_float2(f.z, f.w), hi);
+        }
+      }
+      float* dst = table_s + 4 * s4 * BM + row;
+      dst[0] = lo.x;
+      dst[BM] = lo.y;
+      dst[2 * BM] = hi.x;
+      dst[3 * BM] = hi.y;
+    }
+  } else {
+    for (int s = 0; s < ns; ++s) {
+      float acc = 0.f;
+#pragma unroll
+      for (int pp = 0; pp < kMaxPoses; ++pp)
+        if (pp < np)
+          acc = fmaf(w[pp],
+                     load_any(p.fields, h * p.fields_stride[0] + pp * p.fields_stride[1] + s * p.fields_stride[2],
+                              p.fields_dtype),
+                     acc);
+      table_s[s * BM + row] = acc;
+    }
+  }
+  table_s[ns * BM + row] = 0.f;               // "no bias"
+  table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
+}
+
+// Starts fetching into L2 the Look row that stage_table will read for query
+// token i of (b, h) in a later work item.
+__device__ __forceinline__ void prefetch_table_row(const TcArgs& a, int64_t b, int64_t h, int64_t i) {
+  const SlaParams& p = a.p;
+  if (!a.pose_vec4 || i < 1 || i >= p.seq) return;
+  const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
+  bulk_prefetch_l2(static_cast<const float*>(p.pose) + base, static_cast<uint32_t>(a.n_slots) * 4u);
 }
 
 // S row (64 fp32 scores of this thread's TMEM lane) into t[c] = keys 2c, 2c+1.
@@ -278,6 +422,8 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       mbar_init(&bars->p_full[s], 4);
       mbar_init(&bars->pv_done[s], 1);
     }
+    mbar_init(&bars->sf_ready, 4);
+    mbar_init(&bars->sf_free, 4);
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     mbar_fence_init();
@@ -468,22 +614,75 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       return mbar_wait(&bars->pv_done[t & 1], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax);
     };
     bool ok = true;
+    // SLOT_FIELDS inputs of a work item are fetched one item ahead: the pose
+    // row into w and (sf_vec4) the head's slot values into shared memory,
+    // issued after the previous item's last score tile so that they land
+    // while its epilogue waits for the last PV.  sf_ready: the 4 warps staged
+    // item c's slot values; sf_free: the 4 warps built item c's table (the
+    // staging area may be overwritten).  c counts this CTA's items.
+    float w[kMaxPoses];
+    uint32_t sf_count = 0;
+    auto sf_begin = [&](uint32_t it) -> bool {
+      const uint32_t ibh = it / n_qt;
+      load_pose_row(w, a, ibh / H, ibh % H, static_cast<int64_t>(it % n_qt) * BM + row);
+      if (!a.sf_vec4) return true;
+      if (sf_count > 0 &&
+          !mbar_wait(&bars->sf_free, (sf_count - 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax))
+        return false;
+      stage_slot_fields(table_s, a, ibh % H, row);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sf_ready);
+      return true;
+    };
+    auto sf_finish = [&](int64_t head) -> bool {
+      if (a.sf_vec4 && !mbar_wait(&bars->sf_ready, sf_count & 1, abort_flag, p.status, kDevTimeoutSoftmax))
+        return false;
+      build_table_sf(table_s, a, head, row, w);
+      if (a.sf_vec4) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->sf_free);
+      }
+      ++sf_count;
+      return true;
+    };
+    if (use_bias && a.slot_fields && blockIdx.x < n_items) ok = sf_begin(blockIdx.x);
     for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const uint32_t qt = item % n_qt;
       const uint32_t bh = item / n_qt;
       const int64_t h = bh % H, b = bh / H;
       const int64_t i = static_cast<int64_t>(qt) * BM + row;  // token index of this thread's row
-      if (use_bias) stage_table(table_s, a, b, h, i, row);
+      // Flags of the item's first 64 key tiles, loaded before the table so
+      // that the two memory round trips overlap.
+      uint8_t fl0 = 0, fl1 = 0;
+      if (use_bias) {
+        fl0 = lane < n_kt ? p.slot_tile_flags[qt * n_kt + lane] : 0;
+        fl1 = lane + 32 < n_kt ? p.slot_tile_flags[qt * n_kt + lane + 32] : 0;
+        if (a.slot_fields) {
+          if (!sf_finish(h)) {
+            ok = false;
+            break;
+          }
+        } else {
+          stage_table(table_s, a, b, h, i, row);
+          const uint32_t next = item + gridDim.x;
+          if (next < n_items) {
+            const uint32_t nbh = next / n_qt;
+            prefetch_table_row(a, nbh / H, nbh % H, static_cast<int64_t>(next % n_qt) * BM + row);
+          }
+        }
+      }
       float m = -INFINITY;
       uint64_t tile_mask = 0;  // bit k: key tile (j & ~63) + k carries Look bias for this warp
       for (int64_t j = 0; j < n_kt; ++j, ++k_iter) {
         if (use_bias && (j & 63) == 0) {
           // Each warp gathers the flags of the next 64 key tiles with one ballot pair.
-          const int64_t t0 = j + lane, t1 = j + 32 + lane;
-          const bool f0 = t0 < n_kt && ((p.slot_tile_flags[qt * n_kt + t0] >> warp) & 1);
-          const bool f1 = t1 < n_kt && ((p.slot_tile_flags[qt * n_kt + t1] >> warp) & 1);
-          tile_mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, f0)) |
-                      (static_cast<uint64_t>(__ballot_sync(0xffffffffu, f1)) << 32);
+          if (j > 0) {
+            const int64_t t0 = j + lane, t1 = j + 32 + lane;
+            fl0 = t0 < n_kt ? p.slot_tile_flags[qt * n_kt + t0] : 0;
+            fl1 = t1 < n_kt ? p.slot_tile_flags[qt * n_kt + t1] : 0;
+          }
+          tile_mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, (fl0 >> warp) & 1)) |
+                      (static_cast<uint64_t>(__ballot_sync(0xffffffffu, (fl1 >> warp) & 1)) << 32);
         }
         const uint32_t sb = g & 1;
         if (!mbar_wait(&bars->s_full[sb], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
@@ -563,6 +762,10 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         ++g;
       }
       if (!ok) break;
+      if (use_bias && a.slot_fields && item + gridDim.x < n_items && !sf_begin(item + gridDim.x)) {
+        ok = false;
+        break;
+      }
       // Epilogue: wait for the item's last PV, normalise by the row sum (O column 64), store.
       if (!wait_pv(g - 1)) {
         ok = false;
@@ -714,8 +917,11 @@ int32_t sla_tc_supported(const SlaParams& p) {
   if (p.dtype != 1 && p.dtype != 2) return 0;
   if (p.head_dim != HD) return 0;
   if (p.dense != nullptr) return 0;
-  if (p.bias_mode != 0 && p.bias_mode != 2) return 0;
+  if (p.bias_mode != 0 && p.bias_mode != 2 && p.bias_mode != 3) return 0;
   if (p.bias_mode == 2 && (p.poses < 1 || p.poses > kMaxSlots || !p.slots_packed || !p.slot_tile_flags)) return 0;
+  if (p.bias_mode == 3 && (p.slots < 1 || p.slots > kMaxSlots || p.poses < 1 || p.poses > kMaxPoses ||
+                           !p.slots_packed || !p.slot_tile_flags || !p.fields))
+    return 0;
   if (p.status == nullptr) return 0;
   if (p.seq < 2 || p.seq > (int64_t(1) << 30) || p.batch > (int64_t(1) << 30) || p.heads > (int64_t(1) << 30))
     return 0;
@@ -741,10 +947,25 @@ int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
   a.n_qt = (p.seq + BM - 1) / BM;
   a.n_kt = (p.seq + BN - 1) / BN;
   a.n_items = p.batch * p.heads * a.n_qt;
-  a.n_slots = p.bias_mode == 2 ? static_cast<int32_t>(p.poses) : 0;
+  a.n_slots = p.bias_mode == 2 ? static_cast<int32_t>(p.poses) : (p.bias_mode == 3 ? static_cast<int32_t>(p.slots) : 0);
+  a.slot_fields = p.bias_mode == 3 ? 1 : 0;
+  a.n_poses = p.bias_mode == 3 ? static_cast<int32_t>(p.poses) : 0;
+  a.sf_vec4 = 0;
+  if (p.bias_mode == 3 && p.fields_dtype == 0 && p.fields_stride[2] == 1 && a.n_slots % 4 == 0 &&
+      reinterpret_cast<uintptr_t>(p.fields) % 16 == 0 && p.fields_stride[0] % 4 == 0 && p.fields_stride[1] % 4 == 0)
+    a.sf_vec4 = 1;
   a.table_bytes = table_bytes_for(a.n_slots);
+  a.sf_offset = 0;
+  if (a.sf_vec4) {  // staged slot values after the table rows: P x S fp32
+    a.sf_offset = a.table_bytes / 4;
+    a.table_bytes += static_cast<uint32_t>(a.n_poses * a.n_slots * 4);
+  }
   a.pose_vec4 = 0;
-  if (a.n_slots > 0 && p.pose_dtype == 0 && p.pose_stride[3] == 1 && a.n_slots % 4 == 0 &&
+  if (p.bias_mode == 3 && p.pose_dtype == 0 && p.pose_stride[3] == 1 && a.n_poses % 4 == 0 &&
+      reinterpret_cast<uintptr_t>(p.pose) % 16 == 0 && p.pose_stride[0] % 4 == 0 && p.pose_stride[1] % 4 == 0 &&
+      p.pose_stride[2] % 4 == 0)
+    a.pose_vec4 = 1;
+  if (p.bias_mode == 2 && p.pose_dtype == 0 && p.pose_stride[3] == 1 && a.n_slots % 4 == 0 &&
       reinterpret_cast<uintptr_t>(p.pose) % 16 == 0 && p.pose_stride[0] % 4 == 0 && p.pose_stride[1] % 4 == 0 &&
       p.pose_stride[2] % 4 == 0)
     a.pose_vec4 = 1;

@@ -118,8 +118,15 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
       float* dst = pose_s + (t * LH + h) * LP;
 #pragma unroll
       for (int pp = 0; pp < LP; ++pp) dst[pp] = sc[pp] * inv;
+      if (a.look_pose != nullptr) {
+        float4* g = reinterpret_cast<float4*>(a.look_pose + (row * LH + h) * LP);
+#pragma unroll
+        for (int c = 0; c < LP / 4; ++c)
+          g[c] = make_float4(sc[4 * c] * inv, sc[4 * c + 1] * inv, sc[4 * c + 2] * inv, sc[4 * c + 3] * inv);
+      }
     }
   }
+  if (a.values == nullptr) return;
 
   // Phase 2.  Thread -> (head, quad of 4 slots): the quad's 4 x LP fields stay
   // in registers while the thread walks the CTA's patches (48 FMAs per three
@@ -260,10 +267,11 @@ extern "C" INTP_API intp_status svit_embed_post(const svit_embed_args* a, void* 
   const int64_t columns = static_cast<int64_t>(a->bases) * D + static_cast<int64_t>(LP) * a->look_heads;
   if (a->resp_stride < columns) return INTP_ERR_SHAPE;
   if (!a->resp || !a->token_null || !a->direction_coef || !a->output_bias || !a->cls || !a->pos_embed ||
-      !a->look_null || !a->slot_fields || !a->x || !a->values)
+      !a->look_null || !a->x || (!a->values && !a->look_pose) || (a->values && !a->slot_fields))
     return INTP_ERR_ARGUMENT;
   if (!aligned(a->x, 8)) return INTP_ERR_LAYOUT;
-  if (a->slots % 4 || !aligned(a->slot_fields, 16) || !aligned(a->values, 16)) return INTP_ERR_LAYOUT;
+  if (a->values && (a->slots % 4 || !aligned(a->slot_fields, 16) || !aligned(a->values, 16))) return INTP_ERR_LAYOUT;
+  if (a->look_pose && !aligned(a->look_pose, 16)) return INTP_ERR_LAYOUT;
   const size_t smem = static_cast<size_t>(kPostTokens) * a->look_heads * LP * sizeof(float);
   if (smem > 200 * 1024) return INTP_ERR_SHAPE;
   auto kernel = embed_post_kernel<D, LP>;

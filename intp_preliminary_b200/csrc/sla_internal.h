@@ -15,8 +15,9 @@ struct SlaParams {
   const void* v; int64_t v_stride[4];
   void* out; int64_t out_stride[4];
   float* lse;
-  int32_t bias_mode;
-  int64_t poses;
+  int32_t bias_mode;  // 0 none, 1 fields, 2 slots, 3 slot fields
+  int64_t poses;      // P (modes 1, 3) or number of slots (mode 2)
+  int64_t slots;      // number of slots (mode 3)
   const void* pose; int64_t pose_stride[4]; int32_t pose_dtype;
   const void* fields; int64_t fields_stride[4]; int32_t fields_dtype;
   const uint8_t* slots_packed;

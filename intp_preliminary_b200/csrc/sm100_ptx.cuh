@@ -266,6 +266,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool ab_bf16, bool b_mn_major, 
          | ((m >> 4) << 24);                        // M / 16
 }
 
+// Asynchronous prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------- packed fp32 pairs
 // sm_100 executes two fp32 lanes per instruction with the .f32x2 forms.
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {

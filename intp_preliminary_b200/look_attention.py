@@ -17,6 +17,13 @@ shared by every batch and head and the bias becomes ``pose[b, q, h, slot]``.
 That is the form the tensor-core kernel consumes without ever materialising an
 ``Np x Np`` bias or field tensor.
 
+``fields`` may also be a :class:`LookSlotFields`: fields whose every
+``(Np, Np)`` plane is a per-slot value gathered by such a pair table
+(``fields[h, p, q, k] = values[h, p, slot(q, k)]``), which is how the
+reference model's Look bank builds them (model/deit_tiny_rot_hex_look.py:397-451).
+The bias is then ``sum_p pose[b, q, h, p] * values[h, p, slot(q, k)]``, formed per
+query inside the kernel from the P pose values and the ``(H, P, S)`` slot values.
+
 Every call runs the CUDA kernels of ``libintp_b200.so``; there is no CPU or
 PyTorch fallback.  CPU tensors raise ``ValueError`` like any other input the
 kernels cannot take.
@@ -140,9 +147,40 @@ def _stride4(t: torch.Tensor):
     return _lib._Stride(*[int(s) for s in t.stride()])
 
 
+class LookSlotFields:
+    """Look fields ``(H, P, Np, Np)`` held per slot: ``fields[h, p, q, k] =
+    values[h, p, slot(q, k)]``, zero where the pair has no slot.
+
+    ``slots`` is the :class:`LookSlots` pair table, ``values`` a ``(H, P, S)``
+    floating tensor with ``S = slots.n_slots`` (it may require grad).
+    """
+
+    def __init__(self, slots: LookSlots, values: torch.Tensor) -> None:
+        if not isinstance(slots, LookSlots):
+            raise ValueError("slots must be a LookSlots table")
+        if not isinstance(values, torch.Tensor) or values.ndim != 3 or values.shape[-1] != slots.n_slots:
+            raise ValueError("values must be a (H, P, n_slots) tensor")
+        self.slots = slots
+        self.values = values
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        heads, poses, _ = self.values.shape
+        return (heads, poses, self.slots.patch_count, self.slots.patch_count)
+
+    def dense(self) -> torch.Tensor:
+        """The equivalent ``(H, P, Np, Np)`` field tensor (for checks; Np^2 memory)."""
+        table = torch.from_numpy(self.slots.table.astype(np.int64)).to(self.values.device)
+        none = table == _lib.SLA_SLOT_NONE
+        gathered = self.values[:, :, table.masked_fill(none, 0)]
+        return gathered.masked_fill(none, 0.0)
+
+
 def _validate(q, k, v, pose, fields, dense_bias):
     """The reference's checks, in its order (layers/triton_structured_look_attention.py:298-319)."""
     tensors = [q, k, v, pose] + ([fields] if isinstance(fields, torch.Tensor) else [])
+    if isinstance(fields, LookSlotFields):
+        tensors.append(fields.values)
     if dense_bias is not None:
         tensors.append(dense_bias)
     if not all(isinstance(t, torch.Tensor) and t.is_cuda for t in tensors):
@@ -158,6 +196,11 @@ def _validate(q, k, v, pose, fields, dense_bias):
     if isinstance(fields, LookSlots):
         if fields.n_slots != poses or fields.patch_count != patch_count or fields.heads not in (None, heads):
             raise ValueError("fields shape is inconsistent with pose")
+    elif isinstance(fields, LookSlotFields):
+        if fields.shape != (heads, poses, patch_count, patch_count):
+            raise ValueError("fields shape is inconsistent with pose")
+        if fields.values.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise ValueError("slot values must be float32, float16 or bfloat16")
     elif fields.shape != (heads, poses, patch_count, patch_count):
         raise ValueError("fields shape is inconsistent with pose")
     if dense_bias is not None and dense_bias.shape != (batch, heads, patch_count, patch_count):
@@ -198,6 +241,14 @@ def _forward_args(q, k, v, pose, fields, scale, dense_bias, out, lse, kernel):
         packed, flags = fields.device_packed(device)
         args.bias_mode = _lib.SLA_BIAS_SLOTS
         args.slots_packed, args.slot_tile_flags = packed.data_ptr(), flags.data_ptr()
+    elif isinstance(fields, LookSlotFields):
+        packed, flags = fields.slots.device_packed(device)
+        values = fields.values
+        args.bias_mode = _lib.SLA_BIAS_SLOT_FIELDS
+        args.slots_packed, args.slot_tile_flags = packed.data_ptr(), flags.data_ptr()
+        args.fields, args.fields_dtype = values.data_ptr(), _DTYPE_CODE[values.dtype]
+        args.fields_stride = _lib._Stride(values.stride(0), values.stride(1), values.stride(2), 0)
+        args.slots = fields.slots.n_slots
     else:
         fields_f = fields if fields.dtype in _DTYPE_CODE else fields.float()
         keep.append(fields_f)
@@ -265,6 +316,18 @@ def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale,
     device = q.device
     if grad_out.shape != q.shape or grad_out.device != device:
         raise ValueError("grad_output must match q in shape and device")
+    if isinstance(fields, LookSlotFields):
+        # Through the per-slot values pose . values (the SLOTS form), then the
+        # chain rule back to pose and the slot values.
+        sf = fields.values.float()
+        per_slot = torch.einsum("bqhp,hps->bqhs", pose.float(), sf)
+        want = needs[3] or needs[4]
+        dq, dk, dv, dslot, _, ddense = look_attention_backward(
+            q, k, v, out, lse, grad_out, per_slot, fields.slots, scale=scale, dense_bias=dense_bias,
+            needs=(needs[0], needs[1], needs[2], want, False, needs[5]))
+        dpose = torch.einsum("bqhs,hps->bqhp", dslot, sf).to(pose.dtype) if needs[3] else None
+        dvalues = torch.einsum("bqhp,bqhs->hps", pose.float(), dslot).to(fields.values.dtype) if needs[4] else None
+        return dq, dk, dv, dpose, dvalues, ddense
     grad_out = grad_out.to(q.dtype)
     if grad_out.stride(-1) != 1:
         grad_out = grad_out.contiguous()
@@ -305,34 +368,42 @@ class _StructuredLookAttention(torch.autograd.Function):
     forward keeps its LSE; the backward recomputes P from it on the GPU."""
 
     @staticmethod
-    def forward(ctx, q, k, v, pose, fields, dense_bias, scale):
+    def forward(ctx, q, k, v, pose, fields_t, dense_bias, scale, slots):
+        # fields_t: the dense fields (slots None), empty (LookSlots), or the
+        # (H, P, S) slot values (LookSlotFields).
+        fields = fields_t if slots is None else (slots if fields_t.numel() == 0 else LookSlotFields(slots, fields_t))
         dense = dense_bias if dense_bias.numel() else None
         out, lse = look_attention_forward(q, k, v, pose, fields, scale=scale, dense_bias=dense, want_lse=True)
         ctx.scale = scale
-        ctx.slots = fields if isinstance(fields, LookSlots) else None
+        ctx.slots = slots
         ctx.has_dense = dense is not None
-        saved_fields = fields if ctx.slots is None else q.new_empty(0)
-        ctx.save_for_backward(q, k, v, pose, saved_fields, dense_bias, out, lse)
+        ctx.save_for_backward(q, k, v, pose, fields_t, dense_bias, out, lse)
         return out
 
     @staticmethod
     def backward(ctx, grad_output):
-        q, k, v, pose, fields, dense_bias, out, lse = ctx.saved_tensors
-        fields = ctx.slots if ctx.slots is not None else fields
+        q, k, v, pose, fields_t, dense_bias, out, lse = ctx.saved_tensors
+        slots = ctx.slots
+        fields = fields_t if slots is None else (slots if fields_t.numel() == 0 else LookSlotFields(slots, fields_t))
         needs = ctx.needs_input_grad[:6]
         dq, dk, dv, dpose, dfields, ddense = look_attention_backward(
             q, k, v, out, lse, grad_output, pose, fields, scale=ctx.scale,
             dense_bias=dense_bias if ctx.has_dense else None, needs=needs)
-        return dq, dk, dv, dpose, dfields, ddense, None
+        return dq, dk, dv, dpose, dfields, ddense, None, None
 
 
 def structured_look_attention(q, k, v, pose, fields, *, scale, dense_bias=None):
     """Memory-bounded Look attention forward (layers/triton_structured_look_attention.py:412-424)."""
+    values = fields.values if isinstance(fields, LookSlotFields) else fields
     if not torch.is_grad_enabled() or not any(
-        t.requires_grad for t in (q, k, v, pose, fields, dense_bias) if isinstance(t, torch.Tensor)
+        t.requires_grad for t in (q, k, v, pose, values, dense_bias) if isinstance(t, torch.Tensor)
     ):
         out, _ = look_attention_forward(q, k, v, pose, fields, scale=scale, dense_bias=dense_bias)
         return out
     if dense_bias is None:
         dense_bias = q.new_empty(0)
-    return _StructuredLookAttention.apply(q, k, v, pose, fields, dense_bias, float(scale))
+    if isinstance(fields, LookSlotFields):
+        return _StructuredLookAttention.apply(q, k, v, pose, fields.values, dense_bias, float(scale), fields.slots)
+    if isinstance(fields, LookSlots):
+        return _StructuredLookAttention.apply(q, k, v, pose, q.new_empty(0), dense_bias, float(scale), fields)
+    return _StructuredLookAttention.apply(q, k, v, pose, fields, dense_bias, float(scale), None)

@@ -26,7 +26,10 @@ Forward, per batch of images (B, 3, 224, 224):
    (:357-379) are bilinear samples of each head's 4x12 grid at pair geometry
    that depends only on the pair; pairs with identical sampling weights share
    a slot, so the per-query Look value per slot is pose @ F_slots and the
-   attention kernel reads it through a (195, 195) uint8 slot table.
+   attention kernel reads it through a (195, 195) uint8 slot table.  In
+   bf16 mode the attention takes pose and F_slots themselves
+   (``LookSlotFields``) and forms pose @ F_slots per query tile in shared
+   memory; the (B, 195, 36, S) per-slot values are never written.
 6. 12 pre-norm transformer blocks (layers/mini_vit.py:138-170) whose attention
    is ``look_attention_forward`` (the tensor-core kernel for bf16), final
    LayerNorm and the classifier on the CLS token.
@@ -41,13 +44,14 @@ from __future__ import annotations
 
 import math
 import threading
+from typing import NamedTuple
 
 import numpy as np
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .look_attention import LookSlots, look_attention_forward
+from .look_attention import LookSlotFields, LookSlots, look_attention_forward
 from .share_vit_ops import add_layernorm, embed_post, gather_patches, linear_gelu, linear_residual_layernorm
 
 IMAGE_SIZE = 224
@@ -105,6 +109,15 @@ def _staggered(n_x: int, n_y: int, step_x, step_y, dtype) -> tuple[torch.Tensor,
         xs = torch.cat((xs, extra_x))
         ys = torch.cat((ys, torch.zeros_like(extra_x) + (n_y - 1) * step_y))
     return xs, ys
+
+
+class LookPose(NamedTuple):
+    """Look inputs of the attention layers in SLOT_FIELDS form: ``pose`` (B, N,
+    36, P) after the Look bank's null softmax and ``fields`` (36, P, S), the
+    value of every slot for each head and pose."""
+
+    pose: torch.Tensor
+    fields: torch.Tensor
 
 
 class HexSupport:
@@ -452,11 +465,15 @@ class ShareViTHalf6d3r(nn.Module):
         return hit
 
     @torch.no_grad()
-    def embed_fused(self, image: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def embed_fused(self, image: torch.Tensor, *, per_slot_values: bool = False):
         """bf16 tokenizer + Look bank on the fused kernels: the residual stream
-        x (B, N+1, 192) fp32 with CLS and position embedding, and the per-slot
-        Look values (B, N, 36, S) fp32 - a view of a (B, 36, N, S) buffer, so
-        each head's rows are contiguous.  Same math as ``embed`` + ``look_values``."""
+        x (B, N+1, 192) fp32 with CLS and position embedding, and the Look
+        inputs of the 12 attention layers.  Default: a ``LookPose`` - the Look
+        pose (B, N, 36, 12) after the null softmax plus the (36, 12, S) slot
+        values; each attention forms its per-slot values itself
+        (``LookSlotFields``).  ``per_slot_values=True``: the per-slot Look values
+        (B, N, 36, S) fp32 - a view of a (B, 36, N, S) buffer, so each head's
+        rows are contiguous.  Same math as ``embed`` + ``look_values``."""
         if image.ndim != 4 or tuple(image.shape[1:]) != (IN_CHANS, IMAGE_SIZE, IMAGE_SIZE):
             raise ValueError(f"expected images (B, {IN_CHANS}, {IMAGE_SIZE}, {IMAGE_SIZE})")
         batch, n = image.shape[0], self.num_patches
@@ -465,7 +482,11 @@ class ShareViTHalf6d3r(nn.Module):
         patches = gather_patches(image, self.pixel_index, self.pixel_weight)
         resp = patches @ w.t()
         x = torch.empty(batch, n + 1, EMBED_DIM, dtype=torch.float32, device=image.device)
-        values = torch.empty(batch, LOOK_HEADS, n, fields.shape[-1], dtype=torch.float32, device=image.device)
+        values = look_pose = None
+        if per_slot_values:
+            values = torch.empty(batch, LOOK_HEADS, n, fields.shape[-1], dtype=torch.float32, device=image.device)
+        else:
+            look_pose = torch.empty(batch, n, LOOK_HEADS, 2 * DIRECTIONS, dtype=torch.float32, device=image.device)
         embed_post(resp, batch=batch, patches=n, bases=BASES, directions=DIRECTIONS, look_heads=LOOK_HEADS,
                    look_poses=2 * DIRECTIONS, token_null=self.patch_embed.null_score.detach().float().contiguous(),
                    direction_coef=self.direction_coefficients.contiguous(),
@@ -473,19 +494,31 @@ class ShareViTHalf6d3r(nn.Module):
                    cls=self.cls_token.detach().float().reshape(-1).contiguous(),
                    pos_embed=self.pos_embed.detach().float().reshape(n + 1, EMBED_DIM).contiguous(),
                    look_null=self.look_bank.null_score.detach().float().contiguous(), slot_fields=fields,
-                   x=x, values=values)
-        return x, values.permute(0, 2, 1, 3)
+                   x=x, values=values, look_pose=look_pose)
+        if per_slot_values:
+            return x, values.permute(0, 2, 1, 3)
+        return x, LookPose(look_pose, fields)
+
+    def _layer_look(self, look, layer: int):
+        """(pose, fields) argument pair of attention layer ``layer`` for Look
+        inputs from ``embed_fused``: SLOT_FIELDS form for a ``LookPose``, SLOTS
+        form for per-slot values."""
+        heads = slice(HEADS * layer, HEADS * (layer + 1))
+        if isinstance(look, LookPose):
+            return look.pose[:, :, heads], LookSlotFields(self.look_slots, look.fields[heads])
+        return look[:, :, heads], self.look_slots
 
     @torch.no_grad()
-    def trunk_fused(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool = False,
+    def trunk_fused(self, x: torch.Tensor, values, *, cls_only: bool = False,
                     linears: str = "tcgen05") -> torch.Tensor:
         """The 12 blocks and the final LayerNorm in bf16 on the fused kernels.
         ``linears="tcgen05"``: proj and fc2 are tcgen05 GEMMs whose epilogue adds
         the residual and applies the next LayerNorm, fc1 one whose epilogue applies
         GELU (qkv stays a cuBLAS GEMM).  ``linears="cublas"``: cuBLAS linears with
         separate add + LayerNorm and GELU passes.  Look attention writes
-        token-major output.  ``x`` is updated in place.  Returns the normalised
-        tokens (B, N+1, 192) bf16, or only the CLS rows (B, 192) when ``cls_only``."""
+        token-major output.  ``values`` is the Look input from ``embed_fused``.
+        ``x`` is updated in place.  Returns the normalised tokens (B, N+1, 192)
+        bf16, or only the CLS rows (B, 192) when ``cls_only``."""
         if linears not in ("tcgen05", "cublas"):
             raise ValueError("linears must be 'tcgen05' or 'cublas'")
         if linears == "tcgen05":
@@ -504,11 +537,11 @@ class ShareViTHalf6d3r(nn.Module):
             h = add_layernorm(x, y, blk.norm1.weight, blk.norm1.bias, 1e-6)
             qkv = F.linear(h, w_qkv, b_qkv).view(batch, n1, 3, HEADS, head_dim)
             q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
-            pose_l = values[:, :, HEADS * layer:HEADS * (layer + 1)]
+            pose_l, fields_l = self._layer_look(values, layer)
             if events is not None:
                 start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 start.record()
-            look_attention_forward(q, k, v, pose_l, self.look_slots, scale=scale, out=attn_bhnd)
+            look_attention_forward(q, k, v, pose_l, fields_l, scale=scale, out=attn_bhnd)
             if events is not None:
                 stop.record()
                 events.append((start, stop))
@@ -519,7 +552,7 @@ class ShareViTHalf6d3r(nn.Module):
             return add_layernorm(x[:, 0], y.view(batch, n1, EMBED_DIM)[:, 0], self.norm.weight, self.norm.bias, 1e-6)
         return add_layernorm(x, y, self.norm.weight, self.norm.bias, 1e-6).view(batch, n1, EMBED_DIM)
 
-    def _trunk_tcgen05(self, x: torch.Tensor, values: torch.Tensor, *, cls_only: bool) -> torch.Tensor:
+    def _trunk_tcgen05(self, x: torch.Tensor, values, *, cls_only: bool) -> torch.Tensor:
         batch, n1 = x.shape[0], x.shape[1]
         rows = batch * n1
         head_dim = EMBED_DIM // HEADS
@@ -534,11 +567,11 @@ class ShareViTHalf6d3r(nn.Module):
             w_qkv, b_qkv, w_proj, _, w_fc1, _, w_fc2, _ = weights[layer]
             qkv = F.linear(h, w_qkv, b_qkv).view(batch, n1, 3, HEADS, head_dim)
             q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
-            pose_l = values[:, :, HEADS * layer:HEADS * (layer + 1)]
+            pose_l, fields_l = self._layer_look(values, layer)
             if events is not None:
                 start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 start.record()
-            look_attention_forward(q, k, v, pose_l, self.look_slots, scale=scale, out=attn_bhnd)
+            look_attention_forward(q, k, v, pose_l, fields_l, scale=scale, out=attn_bhnd)
             if events is not None:
                 stop.record()
                 events.append((start, stop))

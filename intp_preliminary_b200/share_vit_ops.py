@@ -57,29 +57,39 @@ def gather_patches(image: torch.Tensor, pixel_index: torch.Tensor, weight: torch
 def embed_post(resp: torch.Tensor, *, batch: int, patches: int, bases: int, directions: int, look_heads: int,
                look_poses: int, token_null: torch.Tensor, direction_coef: torch.Tensor, output_bias: torch.Tensor,
                cls: torch.Tensor, pos_embed: torch.Tensor, look_null: torch.Tensor, slot_fields: torch.Tensor,
-               x: torch.Tensor, values: torch.Tensor) -> None:
-    """Tokens (with CLS and position embedding) into ``x`` (B, N+1, 2*bases) and
-    per-slot Look values into ``values`` (B, look_heads, N, slots), from the
-    bf16 response rows ``resp`` (B*N, >= bases*directions + look_poses*look_heads)."""
+               x: torch.Tensor, values: torch.Tensor | None, look_pose: torch.Tensor | None = None) -> None:
+    """Tokens (with CLS and position embedding) into ``x`` (B, N+1, 2*bases),
+    per-slot Look values into ``values`` (B, look_heads, N, slots) and / or
+    the Look pose into ``look_pose`` (B, N, look_heads, look_poses), from the
+    bf16 response rows ``resp`` (B*N, >= bases*directions + look_poses*look_heads).
+    With ``values=None`` the per-slot products are left to the attention
+    (``LookSlotFields``)."""
     dev = resp.device
     _require(resp.is_cuda and resp.dtype == torch.bfloat16 and resp.ndim == 2 and resp.stride(1) == 1,
              "resp must be a bf16 CUDA matrix with unit column stride")
     _require(resp.shape[0] == batch * patches, "resp must have batch * patches rows")
-    fp32 = (token_null, direction_coef, output_bias, cls, pos_embed, look_null, slot_fields, x, values)
+    _require(values is not None or look_pose is not None, "values or look_pose is needed")
+    fp32 = [t for t in (token_null, direction_coef, output_bias, cls, pos_embed, look_null, slot_fields, x, values,
+                        look_pose) if t is not None]
     for t in fp32:
         _require(t.device == dev and t.dtype == torch.float32 and t.is_contiguous(),
                  "parameters and outputs must be contiguous float32 tensors on resp's device")
     slots = slot_fields.shape[-1]
     _require(slot_fields.shape == (look_heads, look_poses, slots), "slot_fields must be (look_heads, look_poses, S)")
     _require(x.shape == (batch, patches + 1, 2 * bases), "x must be (B, N+1, 2*bases)")
-    _require(values.shape == (batch, look_heads, patches, slots), "values must be (B, look_heads, N, S)")
+    _require(values is None or values.shape == (batch, look_heads, patches, slots),
+             "values must be (B, look_heads, N, S)")
+    _require(look_pose is None or look_pose.shape == (batch, patches, look_heads, look_poses),
+             "look_pose must be (B, N, look_heads, look_poses)")
     a = _lib.SvitEmbedArgs()
     a.batch, a.patches = batch, patches
     a.bases, a.directions, a.look_heads, a.look_poses, a.slots = bases, directions, look_heads, look_poses, slots
     a.resp, a.resp_stride = resp.data_ptr(), resp.stride(0)
     a.token_null, a.direction_coef, a.output_bias = token_null.data_ptr(), direction_coef.data_ptr(), output_bias.data_ptr()
     a.cls, a.pos_embed, a.look_null, a.slot_fields = cls.data_ptr(), pos_embed.data_ptr(), look_null.data_ptr(), slot_fields.data_ptr()
-    a.x, a.values = x.data_ptr(), values.data_ptr()
+    a.x = x.data_ptr()
+    a.values = values.data_ptr() if values is not None else None
+    a.look_pose = look_pose.data_ptr() if look_pose is not None else None
     status = _lib.load().svit_embed_post(ctypes.byref(a), _stream(dev))
     _lib.check(status, "tokenizer / Look-bank post-processing")
 

@@ -15,7 +15,10 @@ Three forms are provided:
   * ``slot_look_attention_np``: numpy, the one-hot-fields case written as a
     gather ``bias[b,h,q,k] = pose[b,q,h,slot(q,k)]`` so large sequences do
     not need an (H, P, Np, Np) tensor.  Mathematically identical to the
-    general form with ``fields = onehot(slots)``.
+    general form with ``fields = onehot(slots)``;
+  * ``slot_fields_dense_np``: expands per-slot field values (the compact form
+    of the reference model's Look fields) into the general ``(H, P, Np, Np)``
+    fields that ``look_attention_np`` takes.
 """
 
 from __future__ import annotations
@@ -99,3 +102,17 @@ def onehot_fields(slots, n_slots: int, heads: int, dtype=np.float32) -> np.ndarr
     for p in range(n_slots):
         fields[p] = slots == p
     return np.broadcast_to(fields, (heads, n_slots, patches, patches)).copy()
+
+
+def slot_fields_dense_np(slot_values, slots, dtype=np.float32) -> np.ndarray:
+    """Dense ``(H, P, Np, Np)`` fields from per-slot values: ``fields[h, p, q, k] =
+    slot_values[h, p, slot(q, k)]``, 0 where the pair has no slot.  This is how
+    the reference model's Look bank fields arise (model/deit_tiny_rot_hex_look.py:397-451
+    passes them to the attention with a per-head pose): each field plane samples a
+    per-head grid at pair geometry, and pairs with the same geometry share a slot."""
+    slot_values = np.asarray(slot_values, dtype=dtype)
+    slots = np.asarray(slots)
+    heads, poses, n_slots = slot_values.shape
+    padded = np.concatenate([slot_values, np.zeros((heads, poses, 1), dtype=dtype)], axis=-1)
+    index = np.where(slots == SLOT_NONE, n_slots, slots).astype(np.int64)
+    return padded[:, :, index]

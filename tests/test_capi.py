@@ -7,6 +7,7 @@ from pathlib import Path
 
 import numpy as np
 import pytest
+import torch
 
 from intp_preliminary_b200 import _lib
 from intp_preliminary_b200.look_attention import LookSlots
@@ -54,7 +55,7 @@ def test_svit_host_side_argument_checks():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.intp_abi_version() == 1
+    assert lib.intp_abi_version() == 2
     assert _lib.status_string(_lib.INTP_OK) == "ok"
     assert "timed out" in _lib.status_string(_lib.INTP_ERR_TIMEOUT)
 
@@ -143,3 +144,39 @@ def test_operators_refuse_cpu_tensors():
         negative_l1_distance(torch.randn(3, 4), torch.randn(2, 4))
     with pytest.raises(ValueError, match="feature"):
         negative_l1_distance(torch.randn(3, 4), torch.randn(2, 5))
+
+
+def test_slot_fields_dense_expansion_matches_oracle():
+    """LookSlotFields.dense() (host tensors) equals the oracle's expansion."""
+    from intp_preliminary_b200 import LookSlotFields
+    from oracle.look_attention import slot_fields_dense_np
+
+    rng = np.random.default_rng(4)
+    table = rng.integers(0, 9, size=(11, 11)).astype(np.uint8)
+    table[rng.random((11, 11)) < 0.3] = 255
+    values = torch.from_numpy(rng.standard_normal((2, 3, 9)).astype(np.float32))
+    look = LookSlotFields(LookSlots(table, 9), values)
+    assert look.shape == (2, 3, 11, 11)
+    np.testing.assert_array_equal(look.dense().numpy(), slot_fields_dense_np(values.numpy(), table))
+    with pytest.raises(ValueError):
+        LookSlotFields(LookSlots(table, 9), values[:, :, :8])
+
+
+def test_slot_fields_mode_argument_checks():
+    """SLOT_FIELDS needs pose, slot values, the packed table and a slot count."""
+    lib = _lib.load()
+    args = _lib.SlaForwardArgs()
+    args.batch, args.heads, args.seq, args.head_dim = 1, 1, 5, 64
+    args.dtype = _lib.INTP_BF16
+    for name in ("q", "k", "v", "out"):
+        setattr(args, name, 16)
+        setattr(args, name + "_stride", _lib._Stride(320, 320, 64, 1))
+    args.bias_mode = _lib.SLA_BIAS_SLOT_FIELDS
+    args.poses = 12
+    args.pose = 16
+    args.slots_packed = args.slot_tile_flags = 16
+    args.slots = 8
+    assert lib.sla_forward(ctypes.byref(args), None) == _lib.INTP_ERR_ARGUMENT  # no slot values
+    args.fields = 16
+    args.slots = 0
+    assert lib.sla_forward(ctypes.byref(args), None) == _lib.INTP_ERR_ARGUMENT  # no slots

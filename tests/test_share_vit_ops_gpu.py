@@ -8,7 +8,7 @@ import torch
 import torch.nn.functional as F
 
 from intp_preliminary_b200 import share_vit_ops as ops
-from intp_preliminary_b200.share_vit import EMBED_DIM, ShareViTHalf6d3r
+from intp_preliminary_b200.share_vit import EMBED_DIM, LookPose, ShareViTHalf6d3r
 
 pytestmark = pytest.mark.gpu
 
@@ -55,13 +55,31 @@ def test_add_layernorm_on_strided_rows(cuda_device):
 
 def test_embed_fused_matches_unfused(model, cuda_device):
     images = torch.randn(4, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(3))
-    x, values = model.embed_fused(images)
+    x, values = model.embed_fused(images, per_slot_values=True)
     tokens, pose = model.embed(images)
     ref_values = model.look_values(pose)
     ref_x = torch.cat((model.cls_token.expand(4, -1, -1), tokens), dim=1) + model.pos_embed
     torch.testing.assert_close(x, ref_x, atol=3e-2, rtol=3e-2)
     torch.testing.assert_close(values, ref_values, atol=3e-2, rtol=3e-2)
     assert torch.equal(x[:, 0], (model.cls_token[0, 0] + model.pos_embed[0, 0]).expand(4, -1))
+    # default: the Look pose and slot values instead of their product
+    x2, look = model.embed_fused(images)
+    assert isinstance(look, LookPose)
+    torch.testing.assert_close(x2, x, atol=0, rtol=0)
+    torch.testing.assert_close(look.pose, pose, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(look.fields, model.slot_fields(), atol=1e-6, rtol=1e-5)
+
+
+def test_look_pose_trunk_matches_per_slot_values(model, cuda_device):
+    """The attention forming pose . slot values itself (SLOT_FIELDS) gives the
+    trunk of the per-slot-values (SLOTS) path."""
+    images = torch.randn(5, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(12))
+    x1, look = model.embed_fused(images)
+    x2, values = model.embed_fused(images, per_slot_values=True)
+    a = model.trunk_fused(x1, look).float()
+    b = model.trunk_fused(x2, values).float()
+    err = (a - b).abs().max().item()
+    assert err <= 2e-2 * b.abs().max().item(), err
 
 
 def test_fused_forward_matches_unfused_bf16(model, cuda_device):
