@@ -412,8 +412,10 @@ def run_ours(args) -> None:
         roofline = _look_roofline(flops, attn_ms, peaks, None, "sla_tc_kernel",
                                   "Look attention inside the model forward (B256 H3 N196 D64 bf16, 68 slots), "
                                   "CUDA events around each of its 12 launches in an eager run of the timed forward")
-        # ours per step: 12 Look attention + hex gather + post-GEMM + 25 add/LayerNorm
-        launches = (12 + 1 + 1 + 25) * args.steps
+        # ours per step: hex gather + post-GEMM + the first LayerNorm, then per block
+        # Look attention, proj + residual + LN, fc1 + GELU, fc2 + residual + LN
+        # (the qkv and tokenizer GEMMs are cuBLAS)
+        launches = (3 + 12 * 4) * args.steps
         # BASELINE config 4 on its own (the N >= 1025 kernel target)
         cfg4 = LookWorkload("look_cfg4", device, seed=99 + ctx.rank)
         cfg4_times = _timed_steps(cfg4.step, max(args.steps, 5), args.warmup, ctx, flush)

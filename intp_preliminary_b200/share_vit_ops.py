@@ -178,3 +178,50 @@ def linear_residual_layernorm(a: torch.Tensor, weight: torch.Tensor, bias: torch
         _ptr(norm_bias), float(eps), _ptr(h), h.stride(0), _status(a.device), _stream(a.device))
     _lib.check(status, "linear + residual + LayerNorm")
     return h
+
+
+def _time_block_linears(batch: int = 256, steps: int = 20) -> dict[str, float]:
+    """The transformer block's three fused linears at the half6d3r shapes
+    (batch x 197 token rows, 192 / 768 features, seeded inputs): 3 warm-up
+    calls each, one more call each (the launches a profiler captures with
+    ``-s 9 -c 3``), then ``steps`` calls each timed with CUDA events.
+    Returns microseconds per call."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rows = batch * 197
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randn(rows, 192, device=dev, generator=g).to(torch.bfloat16)
+    a2 = torch.randn(rows, 768, device=dev, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(768, 192, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    b1 = torch.randn(768, device=dev, generator=g) * 0.1
+    wp = (torch.randn(192, 192, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    w2 = (torch.randn(192, 768, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    bp = torch.randn(192, device=dev, generator=g) * 0.1
+    x = torch.randn(rows, 192, device=dev, generator=g)
+    gamma = torch.rand(192, device=dev, generator=g) + 0.5
+    beta = torch.randn(192, device=dev, generator=g) * 0.1
+    calls = {
+        "fc1 + GELU (K 192, N 768)": lambda: linear_gelu(a, w1, b1),
+        "proj + residual + LayerNorm (K 192, N 192)": lambda: linear_residual_layernorm(a, wp, bp, x, gamma, beta,
+                                                                                       1e-6),
+        "fc2 + residual + LayerNorm (K 768, N 192)": lambda: linear_residual_layernorm(a2, w2, bp, x, gamma, beta,
+                                                                                      1e-6),
+    }
+    for _ in range(4):
+        for fn in calls.values():
+            fn()
+    torch.cuda.synchronize()
+    result = {}
+    for name, fn in calls.items():
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        stop.record()
+        torch.cuda.synchronize()
+        result[name] = start.elapsed_time(stop) / steps * 1000.0
+    return result
+
+
+if __name__ == "__main__":
+    for name, us in _time_block_linears().items():
+        print(f"{name}: {us:.1f} us")
