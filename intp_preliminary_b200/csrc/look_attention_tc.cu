@@ -59,6 +59,7 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 2^8
 constexpr int kMaxSlots = 93;
 constexpr int kMaxPoses = 16;      // SLOT_FIELDS: Look poses per head
+constexpr int kModelPoses = 12;    // the half6d3r Look bank: 2 supports x 6 directions
 template <int KS>
 struct alignas(8) Barriers {
   uint64_t q_full, q_empty;
@@ -244,13 +245,57 @@ __device__ __forceinline__ void load_pose_row(float (&w)[kMaxPoses], const TcArg
   }
 }
 
+// Table columns of one warp in SLOT_FIELDS mode.  Lane (gp = lane / 8,
+// rb = lane % 8) takes rows rb + 8 ((gp + m) % 4), m = 0..3 (their poses by
+// shuffle from the owning lanes) and the 4-slot groups gp, gp + 4, ...: each
+// 16-byte slot-value load feeds four rows (16 independent FMA chains), and for a
+// fixed m the 32 lanes store to 32 different rows (banks).  P, the number of
+// poses, is a compile-time constant (no per-pose tests).
+template <int P>
+__device__ __forceinline__ void build_rows_sf(float* col0, const float4* sf, int groups, int lane, int gp, int rb,
+                                              const float (&w)[kMaxPoses]) {
+  int rows[4];
+  float wr[4][P];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    rows[m] = rb + 8 * ((gp + m) & 3);
+#pragma unroll
+    for (int pp = 0; pp < P; ++pp) wr[m][pp] = __shfl_sync(0xffffffffu, w[pp], rows[m]);
+  }
+  (void)lane;
+  for (int g = gp; g < groups; g += 4) {
+    float acc[4][4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[m][k] = 0.f;
+#pragma unroll
+    for (int pp = 0; pp < P; ++pp) {
+      const float4 f = sf[pp * groups + g];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        acc[m][0] = fmaf(wr[m][pp], f.x, acc[m][0]);
+        acc[m][1] = fmaf(wr[m][pp], f.y, acc[m][1]);
+        acc[m][2] = fmaf(wr[m][pp], f.z, acc[m][2]);
+        acc[m][3] = fmaf(wr[m][pp], f.w, acc[m][3]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      float* dst = col0 + 4 * g * BM + rows[m];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) dst[k * BM] = acc[m][k];
+    }
+  }
+}
+
 // SLOT_FIELDS: the per-query table built from the query's Look pose and the
 // head's slot fields, table[s][row] = log2(e) sum_p pose[b,i-1,h,p]
 // slot_fields[h,p,s] (model/deit_tiny_rot_hex_look.py:397-451 feeds exactly
 // this product to the attention as pose x fields).  With sf_vec4 the slot
-// values come from shared memory (stage_slot_fields; every thread reads the
-// same address), four 4-slot groups at a time so that eight accumulator
-// chains are in flight.
+// values come from shared memory (stage_slot_fields) and each lane computes
+// four rows of its warp (see below); otherwise each thread computes its own
+// row from global memory.
 __device__ __forceinline__ void build_table_sf(float* table_s, const TcArgs& a, int64_t h, int row,
                                                float (&w)[kMaxPoses]) {
   const SlaParams& p = a.p;
@@ -258,50 +303,37 @@ __device__ __forceinline__ void build_table_sf(float* table_s, const TcArgs& a, 
 #pragma unroll
   for (int pp = 0; pp < kMaxPoses; ++pp) w[pp] *= kLog2e;
   if (a.sf_vec4) {
+    // A warp builds its own 32 table columns.  Lane (gp = lane / 8, rb = lane % 8)
+    // takes rows rb + 8 ((gp + m) % 4), m = 0..3 (their poses by shuffle from the
+    // owning lanes), and the 4-slot groups gp, gp + 4, ...: each 16-byte slot-value
+    // load feeds four rows, and for a fixed m the 32 lanes store to 32 different
+    // rows (banks).
     const float4* sf = reinterpret_cast<const float4*>(table_s + a.sf_offset);
     const int groups = ns / 4;
-    int s4 = 0;
-    for (; s4 + 4 <= groups; s4 += 4) {
-      float2 acc[8];
+    const int lane = row & 31, gp = lane >> 3, rb = lane & 7;
+    float* col0 = table_s + (row - lane);  // column of the warp's first row
+    if (np == kModelPoses) {
+      build_rows_sf<kModelPoses>(col0, sf, groups, lane, gp, rb, w);
+    } else {
+      // other pose counts: each thread its own row, one 4-slot group at a time
+      for (int g = 0; g < groups; ++g) {
+        float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc[u] = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int pp = 0; pp < kMaxPoses; ++pp) {
-        if (pp < np) {
-          const float2 wp = make_float2(w[pp], w[pp]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float4 f = sf[pp * groups + s4 + u];
-            acc[2 * u] = fma2(wp, make_float2(f.x, f.y), acc[2 * u]);
-            acc[2 * u + 1] = fma2(wp, make_float2(f.z, f.w), acc[2 * u + 1]);
+        for (int pp = 0; pp < kMaxPoses; ++pp) {
+          if (pp < np) {
+            const float4 f = sf[pp * groups + g];
+            lo = fma2(make_float2(w[pp], w[pp]), make_float2(f.x, f.y), lo);
+            hi = fma2(make_float2(w[pp], w[pp]), make_float2(f.z, f.w), hi);
           }
         }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float* dst = table_s + 4 * (s4 + u) * BM + row;
-        dst[0] = acc[2 * u].x;
-        dst[BM] = acc[2 * u].y;
-        dst[2 * BM] = acc[2 * u + 1].x;
-        dst[3 * BM] = acc[2 * u + 1].y;
+        float* dst = col0 + 4 * g * BM + lane;
+        dst[0] = lo.x;
+        dst[BM] = lo.y;
+        dst[2 * BM] = hi.x;
+        dst[3 * BM] = hi.y;
       }
     }
-    for (; s4 < groups; ++s4) {
-      float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int pp = 0; pp < kMaxPoses; ++pp) {
-        if (pp < np) {
-          const float4 f = sf[pp * groups + s4];
-          lo = fma2(make_float2(w[pp], w[pp]), make_float2(f.x, f.y), lo);
-          hi = fma2(make_float2(w[pp], w[pp]), make_float2(f.z, f.w), hi);
-        }
-      }
-      float* dst = table_s + 4 * s4 * BM + row;
-      dst[0] = lo.x;
-      dst[BM] = lo.y;
-      dst[2 * BM] = hi.x;
-      dst[3 * BM] = hi.y;
-    }
+    __syncwarp();
   } else {
     for (int s = 0; s < ns; ++s) {
       float acc = 0.f;
