@@ -94,8 +94,13 @@ INTP_API intp_status svit_add_layernorm(float* x, int64_t x_stride, const void* 
  * svit_linear_gelu: out = bf16(GELU(C)) with the exact error function
  *   (nn.GELU()); out_features % 256 == 0; out row stride % 8 == 0.
  * svit_linear_residual_layernorm: x += C (x float32, updated in place), then
- *   h = bf16(LayerNorm(x) * gamma + beta); dim (= out_features) == 192.     */
+ *   h = bf16(LayerNorm(x) * gamma + beta); dim (= out_features) == 192.
+ * svit_linear_bias: out = bf16(C) (the attention's qkv projection,
+ *   layers/mini_vit.py:68); out_features % 192 == 0; out row stride % 8 == 0. */
 INTP_API intp_status svit_linear_gelu(const void* a, int64_t a_stride, int64_t rows, int32_t in_features,
+                                      const void* weight, const float* bias, int32_t out_features, void* out,
+                                      int64_t out_stride, int32_t* status, void* stream);
+INTP_API intp_status svit_linear_bias(const void* a, int64_t a_stride, int64_t rows, int32_t in_features,
                                       const void* weight, const float* bias, int32_t out_features, void* out,
                                       int64_t out_stride, int32_t* status, void* stream);
 INTP_API intp_status svit_linear_residual_layernorm(const void* a, int64_t a_stride, int64_t rows,

@@ -49,6 +49,7 @@ SHARE_VIT_SYMBOLS = (
     "svit_embed_post",
     "svit_add_layernorm",
     "svit_linear_gelu",
+    "svit_linear_bias",
     "svit_linear_residual_layernorm",
 )
 
@@ -161,6 +162,8 @@ def load() -> ctypes.CDLL:
         lib.svit_add_layernorm.restype = _i32
         lib.svit_linear_gelu.argtypes = [_vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp]
         lib.svit_linear_gelu.restype = _i32
+        lib.svit_linear_bias.argtypes = [_vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp]
+        lib.svit_linear_bias.restype = _i32
         lib.svit_linear_residual_layernorm.argtypes = [_vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp,
                                                        ctypes.c_float, _vp, _i64, _vp, _vp]
         lib.svit_linear_residual_layernorm.restype = _i32

@@ -3,6 +3,7 @@
 //
 //   C[M, N] = A[M, K] W[N, K]^T + bias     (bf16 operands, fp32 accumulation in TMEM)
 //   GELU epilogue:      out = bf16(GELU_erf(C))                       (MLP fc1)
+//   bias epilogue:      out = bf16(C)                                  (attention qkv)
 //   residual + LN:      x += C (fp32);  h = bf16(LayerNorm(x))         (attention proj, MLP fc2)
 // so the MLP's 768-wide activation is written once (by fc1, already
 // activated) and the residual stream is read and written once per sub-block,
@@ -33,13 +34,13 @@ constexpr uint32_t kASlab = kGBM * kGBK * 2;       // 16 KB
 // accumulator buffer for GELU (each takes half of the tile's columns), one for
 // LayerNorm (a row's statistics stay inside one thread).
 template <int EPI>
-__host__ __device__ constexpr int epi_groups_per_tile() { return EPI == 0 ? 2 : 1; }
+__host__ __device__ constexpr int epi_groups_per_tile() { return EPI == 1 ? 1 : 2; }
 template <int EPI>
 __host__ __device__ constexpr int gemm_threads() { return 64 + 2 * epi_groups_per_tile<EPI>() * 128; }
-constexpr int kEpiGelu = 0, kEpiResidualLN = 1;
+constexpr int kEpiGelu = 0, kEpiResidualLN = 1, kEpiBias = 2;
 // Per epilogue warp, in 32-bit words: GELU two 32 x 32 bf16 blocks; LN two 32 x 32 fp32 residual chunks.
 template <int EPI>
-__host__ __device__ constexpr int stage_words() { return EPI == 0 ? 1024 : 2048; }
+__host__ __device__ constexpr int stage_words() { return EPI == 1 ? 2048 : 1024; }
 constexpr int kMaxGeluN = 4096;         // GELU bias columns kept in shared memory
 constexpr uint32_t kBarrierBytes = 256;  // room reserved for the barrier block
 
@@ -156,7 +157,7 @@ __device__ __forceinline__ int fstage_index(int row, int col) {
 // GELU epilogue of one warp: 32 rows x NT columns from TMEM (row = lane),
 // 32 columns per step; the next step's TMEM load is in flight while this one
 // computes, and the accumulator is released as soon as the last load landed.
-template <int NT>
+template <int NT, bool GELU>
 __device__ __forceinline__ void epilogue_gelu(uint32_t acc, const float* sbias, uint32_t* stage, int lane,
                                               __nv_bfloat16* out, int64_t out_stride, int64_t wrow0, int64_t rows,
                                               uint64_t* acc_empty) {
@@ -182,8 +183,10 @@ __device__ __forceinline__ void epilogue_gelu(uint32_t acc, const float* sbias, 
       const float4 bb = reinterpret_cast<const float4*>(sbias + 32 * s)[q];
       const uint32_t* r = q < 4 ? lo[b] : hi[b];
       const int j = 4 * (q & 3);
-      w[2 * q] = gelu_bf16x2(add2(f2(r[j], r[j + 1]), make_float2(bb.x, bb.y)));
-      w[2 * q + 1] = gelu_bf16x2(add2(f2(r[j + 2], r[j + 3]), make_float2(bb.z, bb.w)));
+      const float2 v0 = add2(f2(r[j], r[j + 1]), make_float2(bb.x, bb.y));
+      const float2 v1 = add2(f2(r[j + 2], r[j + 3]), make_float2(bb.z, bb.w));
+      w[2 * q] = GELU ? gelu_bf16x2(v0) : pack_bf16x2(v0.x, v0.y);
+      w[2 * q + 1] = GELU ? gelu_bf16x2(v1) : pack_bf16x2(v1.x, v1.y);
     }
     uint32_t* sb = stage + 512 * b;
     stage_row_bf16(sb, lane, w);
@@ -390,7 +393,7 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
   }
   // epilogue parameters in shared memory: GELU bias (N), or LN bias | gamma | beta (NT each)
   float* sparams = reinterpret_cast<float*>(smem + STAGES * kStage + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4);
-  if (EPI == kEpiGelu) {
+  if (EPI != kEpiResidualLN) {
     for (int i = threadIdx.x; i < g.N; i += gemm_threads<EPI>()) sparams[i] = g.bias[i];
   } else {
     for (int i = threadIdx.x; i < NT; i += gemm_threads<EPI>()) {
@@ -497,13 +500,14 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       const int32_t n0 = static_cast<int32_t>((t % g.n_tiles_n) * NT);
       const uint32_t acc = lane_base + e * NT + col0;
       const int64_t wrow0 = (t / g.n_tiles_n) * kGBM + (warp & 3) * 32;  // first row of this warp
-      if (EPI == kEpiGelu) {
+      if (EPI != kEpiResidualLN) {
         if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        epilogue_gelu<kCols>(acc, sparams + n0 + col0, stage, lane, g.out + n0 + col0, g.out_stride, wrow0, g.M,
+        epilogue_gelu<kCols, EPI == kEpiGelu>(acc, sparams + n0 + col0, stage, lane, g.out + n0 + col0, g.out_stride,
+                                              wrow0, g.M,
                              &bars->acc_empty[e]);
       } else {
         // The residual rows are fetched into L2, and their first 32 columns
@@ -562,7 +566,7 @@ intp_status launch_gemm(const void* a, int64_t a_stride, const void* w, GemmArgs
     return INTP_ERR_LAUNCH;
   auto kernel = gemm_epilogue_kernel<NT, STAGES, EPI>;
   static_assert(sizeof(GemmBarriers<STAGES>) <= kBarrierBytes, "barrier block");
-  const size_t params = EPI == kEpiGelu ? static_cast<size_t>(g.N) : 3 * NT;
+  const size_t params = EPI != kEpiResidualLN ? static_cast<size_t>(g.N) : 3 * NT;
   const size_t smem = 1024 + STAGES * (kASlab + NT * kGBK * 2) + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4 + params * 4;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
@@ -602,6 +606,27 @@ extern "C" INTP_API intp_status svit_linear_gelu(const void* a, int64_t a_stride
   g.out_stride = out_stride;
   g.status = status;
   return launch_gemm<256, 3, kEpiGelu>(a, a_stride, weight, g, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" INTP_API intp_status svit_linear_bias(const void* a, int64_t a_stride, int64_t rows, int32_t in_features,
+                                                 const void* weight, const float* bias, int32_t out_features,
+                                                 void* out, int64_t out_stride, int32_t* status, void* stream) {
+  if (rows < 0 || in_features < 1 || out_features < 1) return INTP_ERR_SHAPE;
+  if (rows == 0) return INTP_OK;
+  if (out_features > kMaxGeluN) return INTP_ERR_UNSUPPORTED;
+  if (!a || !weight || !bias || !out || !status) return INTP_ERR_ARGUMENT;
+  if (a_stride < in_features || out_stride < out_features || out_stride % 8 || !aligned16(out) || !aligned16(bias))
+    return INTP_ERR_LAYOUT;
+  if (!device_is_sm100()) return INTP_ERR_ARCH;
+  GemmArgs g{};
+  g.M = rows;
+  g.N = out_features;
+  g.K = in_features;
+  g.bias = bias;
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.out_stride = out_stride;
+  g.status = status;
+  return launch_gemm<192, 3, kEpiBias>(a, a_stride, weight, g, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" INTP_API intp_status svit_linear_residual_layernorm(const void* a, int64_t a_stride, int64_t rows,

@@ -52,7 +52,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .look_attention import LookSlotFields, LookSlots, look_attention_forward
-from .share_vit_ops import add_layernorm, embed_post, gather_patches, linear_gelu, linear_residual_layernorm
+from .share_vit_ops import (add_layernorm, embed_post, gather_patches, linear_bias, linear_gelu,
+                            linear_residual_layernorm)
 
 IMAGE_SIZE = 224
 IN_CHANS = 3
@@ -345,6 +346,10 @@ class ShareViTHalf6d3r(nn.Module):
         # When set to a list, forward() appends (start, stop) CUDA events around
         # every attention launch (used by the benchmark to time the kernel in place).
         self.attention_events: list | None = None
+        # When set to a list, the bf16 forward appends each layer's attention
+        # arguments (q, k, v as views of a copy of that layer's qkv buffer, pose,
+        # fields, scale) so that the launches can be replayed on their own.
+        self.attention_inputs: list | None = None
 
     # ------------------------------------------------------------------ weights
     def init_weights(self, seed: int = 0, look_grid_std: float = 0.02) -> "ShareViTHalf6d3r":
@@ -514,7 +519,7 @@ class ShareViTHalf6d3r(nn.Module):
         """The 12 blocks and the final LayerNorm in bf16 on the fused kernels.
         ``linears="tcgen05"``: proj and fc2 are tcgen05 GEMMs whose epilogue adds
         the residual and applies the next LayerNorm, fc1 one whose epilogue applies
-        GELU (qkv stays a cuBLAS GEMM).  ``linears="cublas"``: cuBLAS linears with
+        GELU, qkv one with only the bias.  ``linears="cublas"``: cuBLAS linears with
         separate add + LayerNorm and GELU passes.  Look attention writes
         token-major output.  ``values`` is the Look input from ``embed_fused``.
         ``x`` is updated in place.  Returns the normalised tokens (B, N+1, 192)
@@ -565,9 +570,13 @@ class ShareViTHalf6d3r(nn.Module):
         h = add_layernorm(x, None, self.blocks[0].norm1.weight, self.blocks[0].norm1.bias, 1e-6)
         for layer, blk in enumerate(self.blocks):
             w_qkv, b_qkv, w_proj, _, w_fc1, _, w_fc2, _ = weights[layer]
-            qkv = F.linear(h, w_qkv, b_qkv).view(batch, n1, 3, HEADS, head_dim)
+            qkv = linear_bias(h, w_qkv, blk.attn.qkv.bias).view(batch, n1, 3, HEADS, head_dim)
             q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
             pose_l, fields_l = self._layer_look(values, layer)
+            if self.attention_inputs is not None:
+                kept = qkv.clone()
+                self.attention_inputs.append(
+                    tuple(kept[:, :, i].permute(0, 2, 1, 3) for i in range(3)) + (pose_l, fields_l, scale))
             if events is not None:
                 start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 start.record()

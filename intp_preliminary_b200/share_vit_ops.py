@@ -157,6 +157,20 @@ def linear_gelu(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> to
     return out
 
 
+def linear_bias(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """``bf16(a @ weight.T + bias)`` on the tcgen05 GEMM (the attention's qkv
+    projection).  a (rows, K) bf16, weight (N, K) bf16 with N % 192 == 0, bias (N,) fp32."""
+    _linear_checks(a, weight, bias)
+    rows, k = a.shape
+    n = weight.shape[0]
+    _require(n % 192 == 0, "out_features must be a multiple of 192")
+    out = torch.empty(rows, n, dtype=torch.bfloat16, device=a.device)
+    status = _lib.load().svit_linear_bias(_ptr(a), a.stride(0), rows, k, _ptr(weight), _ptr(bias), n, _ptr(out),
+                                          out.stride(0), _status(a.device), _stream(a.device))
+    _lib.check(status, "linear + bias")
+    return out
+
+
 def linear_residual_layernorm(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, x: torch.Tensor,
                               norm_weight: torch.Tensor, norm_bias: torch.Tensor, eps: float) -> torch.Tensor:
     """``x += a @ weight.T + bias`` (x float32, in place) and return

@@ -115,6 +115,18 @@ def test_linear_gelu_matches_torch(cuda_device, rows):
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("rows,n", [(1, 576), (130, 192), (4096 + 77, 576)])
+def test_linear_bias_matches_torch(cuda_device, rows, n):
+    g = torch.Generator(cuda_device).manual_seed(rows + n)
+    a = torch.randn(rows, 192, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, 192, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+    b = torch.randn(n, device=cuda_device, generator=g) * 0.1
+    out = ops.linear_bias(a, w, b)
+    ref = a.float() @ w.float().t() + b
+    assert out.dtype == torch.bfloat16 and out.shape == (rows, n)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+
 @pytest.mark.parametrize("rows,k", [(1, 192), (130, 192), (4096 + 77, 768)])
 def test_linear_residual_layernorm_matches_torch(cuda_device, rows, k):
     g = torch.Generator(cuda_device).manual_seed(rows + k)
