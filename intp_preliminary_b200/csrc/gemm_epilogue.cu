@@ -129,12 +129,16 @@ __device__ __forceinline__ void stage_row_bf16(uint32_t* stage, int row, const u
 __device__ __forceinline__ void store_staged_bf16(const uint32_t* stage, int lane, __nv_bfloat16* dst, int64_t stride,
                                                   int64_t row0, int64_t rows) {
   const int q = lane & 3;
+  uint4 val[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int rr = 8 * j + (lane >> 2);
-    const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 16 + 4 * (q ^ ((rr >> 1) & 3)));
-    const int64_t m = row0 + rr;
-    if (m < rows) *reinterpret_cast<uint4*>(dst + m * stride + 8 * q) = val;
+    val[j] = *reinterpret_cast<const uint4*>(stage + rr * 16 + 4 * (q ^ ((rr >> 1) & 3)));
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t m = row0 + 8 * j + (lane >> 2);
+    if (m < rows) *reinterpret_cast<uint4*>(dst + m * stride + 8 * q) = val[j];
   }
 }
 
@@ -260,18 +264,25 @@ __device__ __forceinline__ void epilogue_residual_ln(uint32_t acc, const float* 
     tmem_wait_ld();
     reg_fence16(lo);
     reg_fence16(hi);
+    // all loads of the row first, then the stores (the cells are written in place)
+    float4 xv[8], bb[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      xv[q] = *reinterpret_cast<const float4*>(buf + fstage_index(lane, 4 * q));
+      bb[q] = reinterpret_cast<const float4*>(sbias + c)[q];
+    }
     float2 p[16];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      float4* cell = reinterpret_cast<float4*>(buf + fstage_index(lane, 4 * q));
-      const float4 xv = *cell;
-      const float4 bb = reinterpret_cast<const float4*>(sbias + c)[q];
       const uint32_t* r = q < 4 ? lo : hi;
       const int j = 4 * (q & 3);
-      p[2 * q] = add2(add2(f2(r[j], r[j + 1]), make_float2(bb.x, bb.y)), make_float2(xv.x, xv.y));
-      p[2 * q + 1] = add2(add2(f2(r[j + 2], r[j + 3]), make_float2(bb.z, bb.w)), make_float2(xv.z, xv.w));
-      *cell = make_float4(p[2 * q].x, p[2 * q].y, p[2 * q + 1].x, p[2 * q + 1].y);
+      p[2 * q] = add2(add2(f2(r[j], r[j + 1]), make_float2(bb[q].x, bb[q].y)), make_float2(xv[q].x, xv[q].y));
+      p[2 * q + 1] = add2(add2(f2(r[j + 2], r[j + 3]), make_float2(bb[q].z, bb[q].w)), make_float2(xv[q].z, xv[q].w));
     }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4*>(buf + fstage_index(lane, 4 * q)) =
+          make_float4(p[2 * q].x, p[2 * q].y, p[2 * q + 1].x, p[2 * q + 1].y);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       lo[2 * k] = __float_as_uint(p[k].x);
@@ -284,11 +295,13 @@ __device__ __forceinline__ void epilogue_residual_ln(uint32_t acc, const float* 
     __syncwarp();
     {  // v back to the residual stream: 4 rows x 128 bytes per instruction
       const int q = lane & 7;
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const float4*>(buf + fstage_index(4 * j + (lane >> 3), 4 * q));
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int r = 4 * j + (lane >> 3);
-        const float4 v = *reinterpret_cast<const float4*>(buf + fstage_index(r, 4 * q));
-        if (wrow0 + r < rows) *reinterpret_cast<float4*>(x + (wrow0 + r) * x_stride + c + 4 * q) = v;
+        if (wrow0 + r < rows) *reinterpret_cast<float4*>(x + (wrow0 + r) * x_stride + c + 4 * q) = v[j];
       }
     }
     // step statistics: pairwise sums, then the squared deviations about the step mean
@@ -309,9 +322,12 @@ __device__ __forceinline__ void epilogue_residual_ln(uint32_t acc, const float* 
       mean = mb;
       m2 = m2b;
     } else {
+      // weight of the merge: 32 new values on top of 32 s (approximate reciprocal:
+      // statistics only)
+      const float kNew = __fdividef(1.f, static_cast<float>(s + 1));
       const float delta = mb - mean;
-      mean = fmaf(delta, 32.f / (c + 32), mean);
-      m2 += fmaf(delta * delta, (32.f * c) / (c + 32), m2b);
+      mean = fmaf(delta, kNew, mean);
+      m2 += fmaf(delta * delta, 32.f * s * kNew, m2b);
     }
     __syncwarp();
   }
