@@ -67,6 +67,7 @@ struct GemmBarriers {
   uint64_t full[STAGES], empty[STAGES];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t drain;
+  uint64_t params;  // the epilogue parameters have landed in shared memory
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -400,23 +401,13 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       mbar_init(&bars->acc_empty[b], 4 * epi_groups_per_tile<EPI>());
     }
     mbar_init(&bars->drain, 1);
+    mbar_init(&bars->params, 1);
     bars->abort = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
-  }
-  // epilogue parameters in shared memory: GELU bias (N), or LN bias | gamma | beta (NT each)
-  float* sparams = reinterpret_cast<float*>(smem + STAGES * kStage + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4);
-  if (EPI != kEpiResidualLN) {
-    for (int i = threadIdx.x; i < g.N; i += gemm_threads<EPI>()) sparams[i] = g.bias[i];
-  } else {
-    for (int i = threadIdx.x; i < NT; i += gemm_threads<EPI>()) {
-      sparams[i] = g.bias[i];
-      sparams[NT + i] = g.gamma[i];
-      sparams[2 * NT + i] = g.beta[i];
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -502,6 +493,23 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     }
   } else {
     // ------------------------------------------------------------ epilogue warpgroups
+    // Parameters into shared memory (GELU / bias: N bias values; LN: bias | gamma |
+    // beta, NT each) by bulk copies that land while the first tile accumulates;
+    // every epilogue thread waits for them (bounded) before its first tile.
+    float* sparams = reinterpret_cast<float*>(smem + STAGES * kStage + kBarrierBytes +
+                                              8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4);
+    if (threadIdx.x == 64) {
+      if (EPI != kEpiResidualLN) {
+        mbar_arrive_expect_tx(&bars->params, static_cast<uint32_t>(g.N) * 4u);
+        bulk_load(sparams, g.bias, static_cast<uint32_t>(g.N) * 4u, &bars->params);
+      } else {
+        mbar_arrive_expect_tx(&bars->params, 3u * NT * 4u);
+        bulk_load(sparams, g.bias, NT * 4u, &bars->params);
+        bulk_load(sparams + NT, g.gamma, NT * 4u, &bars->params);
+        bulk_load(sparams + 2 * NT, g.beta, NT * 4u, &bars->params);
+      }
+    }
+    bool params_ready = false;
     constexpr int kSplit = epi_groups_per_tile<EPI>();
     constexpr int kCols = NT / kSplit;                      // columns per group
     const int grp = (warp - 2) >> 2;
@@ -522,6 +530,13 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
           break;
         }
         tc_fence_after();
+        if (!params_ready) {
+          if (!mbar_wait(&bars->params, 0, abort_flag, g.status, kDevTimeoutSoftmax)) {
+            ok = false;
+            break;
+          }
+          params_ready = true;
+        }
         epilogue_gelu<kCols, EPI == kEpiGelu>(acc, sparams + n0 + col0, stage, lane, g.out + n0 + col0, g.out_stride,
                                               wrow0, g.M,
                              &bars->acc_empty[e]);
@@ -537,12 +552,24 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
           break;
         }
         tc_fence_after();
+        if (!params_ready) {
+          if (!mbar_wait(&bars->params, 0, abort_flag, g.status, kDevTimeoutSoftmax)) {
+            cp_async_wait<0>();
+            ok = false;
+            break;
+          }
+          params_ready = true;
+        }
         epilogue_residual_ln<NT>(acc, sparams, xbuf, lane, g.x, g.x_stride, g.eps, g.h, g.h_stride, wrow0, g.M,
                                  &bars->acc_empty[e]);
       }
     }
   }
 
+  if (threadIdx.x == 64) {  // the parameter copy has landed before the CTA exits
+    volatile int32_t no_abort = 0;
+    mbar_wait(&bars->params, 0, &no_abort, g.status, kDevTimeoutDrain);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
