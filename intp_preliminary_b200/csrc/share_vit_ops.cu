@@ -53,7 +53,9 @@ __device__ __forceinline__ float bf16_at(const __nv_bfloat16* p, int64_t i) { re
 // values[b, h, n, s] = sum_p pose[row, h, p] * fields[h, p, s] with the head's
 // fields in shared memory and each thread keeping one slot's column in
 // registers while it walks the CTA's patches.
-template <int D, int LP>
+// VALUES: also the per-slot Look values (phase 2); without it the kernel writes
+// x and the Look pose only and compiles without the phase-2 registers.
+template <int D, int LP, bool VALUES>
 __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_embed_args a) {
   extern __shared__ __align__(16) float smem_post[];
   const int LH = a.look_heads, S = a.slots;
@@ -115,9 +117,11 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
         sum += sc[pp];
       }
       const float inv = 1.f / sum;
-      float* dst = pose_s + (t * LH + h) * LP;
+      if (VALUES) {  // staged for the per-slot products of phase 2
+        float* dst = pose_s + (t * LH + h) * LP;
 #pragma unroll
-      for (int pp = 0; pp < LP; ++pp) dst[pp] = sc[pp] * inv;
+        for (int pp = 0; pp < LP; ++pp) dst[pp] = sc[pp] * inv;
+      }
       if (a.look_pose != nullptr) {
         float4* g = reinterpret_cast<float4*>(a.look_pose + (row * LH + h) * LP);
 #pragma unroll
@@ -126,7 +130,9 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
       }
     }
   }
-  if (a.values == nullptr) return;
+  if constexpr (!VALUES) {
+    return;
+  } else {
 
   // Phase 2.  Thread -> (head, quad of 4 slots): the quad's 4 x LP fields stay
   // in registers while the thread walks the CTA's patches (48 FMAs per three
@@ -170,6 +176,7 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
       }
       *reinterpret_cast<float4*>(a.values + base + head_off) = v;
     }
+  }
   }
 }
 
@@ -272,9 +279,11 @@ extern "C" INTP_API intp_status svit_embed_post(const svit_embed_args* a, void* 
   if (!aligned(a->x, 8)) return INTP_ERR_LAYOUT;
   if (a->values && (a->slots % 4 || !aligned(a->slot_fields, 16) || !aligned(a->values, 16))) return INTP_ERR_LAYOUT;
   if (a->look_pose && !aligned(a->look_pose, 16)) return INTP_ERR_LAYOUT;
-  const size_t smem = static_cast<size_t>(kPostTokens) * a->look_heads * LP * sizeof(float);
+  // the pose staging only serves the per-slot products (values); without them
+  // the kernel needs no shared memory and more CTAs fit on an SM
+  const size_t smem = a->values ? static_cast<size_t>(kPostTokens) * a->look_heads * LP * sizeof(float) : 0;
   if (smem > 200 * 1024) return INTP_ERR_SHAPE;
-  auto kernel = embed_post_kernel<D, LP>;
+  auto kernel = a->values ? embed_post_kernel<D, LP, true> : embed_post_kernel<D, LP, false>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return INTP_ERR_LAUNCH;
   const int64_t blocks = (a->batch * a->patches + kPostTokens - 1) / kPostTokens;
