@@ -42,6 +42,30 @@ INTP_API intp_status svit_gather_patches(const float* image, int64_t batch, int6
                                          const int32_t* pixel_index, const float* weight, int64_t patches,
                                          int64_t features, void* out, void* stream);
 
+/* The same gather through shared memory.  Patches are taken in groups of
+ * group_patches consecutive ones (the last group may hold fewer); the 16-byte
+ * image units (4 pixels; unit u holds offsets 4u .. 4u + 3) that a group
+ * reads are listed once, sorted, in stage_offset[stage_begin[g] ..
+ * stage_begin[g + 1]), and local_index[n, f] is the float position of
+ * pixel_index[n, f] among its group's units (4 * rank + offset % 4).  One CTA
+ * per (image, group) copies the listed units into shared memory, then writes
+ * the group's rows from there: the image is read with coalesced 16-byte
+ * copies instead of one scattered load per feature.  image and image_elems
+ * must be 16-byte aligned / a multiple of 4.  The plan depends on the patch
+ * geometry only; the caller builds it once from pixel_index.                */
+typedef struct svit_gather_plan {
+  const int32_t* stage_offset; /* sum of the group counts, int32 units, each in [0, image_elems / 4) */
+  const int32_t* stage_begin;  /* (groups + 1), stage_begin[0] = 0, non-decreasing */
+  const int16_t* local_index;  /* (patches, features) in [0, 4 * group count), 16-byte aligned */
+  int64_t groups;              /* ceil(patches / group_patches) */
+  int64_t group_patches;
+  int64_t max_stage;           /* largest group count; max_stage * 16 bytes <= 227 KB */
+} svit_gather_plan;
+
+INTP_API intp_status svit_gather_patches_staged(const float* image, int64_t batch, int64_t image_elems,
+                                                const svit_gather_plan* plan, const float* weight,
+                                                int64_t patches, int64_t features, void* out, void* stream);
+
 /* Geometry of the post-GEMM step (one response row per patch).
  * resp row layout (bf16): [bases x directions tokenizer scores |
  * for each support s: look_heads x directions Look-bank responses], so Look

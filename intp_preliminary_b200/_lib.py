@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
 # Every symbol include/intp_share_vit.h declares.
 SHARE_VIT_SYMBOLS = (
     "svit_gather_patches",
+    "svit_gather_patches_staged",
     "svit_embed_post",
     "svit_add_layernorm",
     "svit_linear_gelu",
@@ -114,6 +115,15 @@ class SvitEmbedArgs(ctypes.Structure):
     ]
 
 
+class SvitGatherPlan(ctypes.Structure):
+    """Mirror of ``svit_gather_plan`` (include/intp_share_vit.h)."""
+
+    _fields_ = [
+        ("stage_offset", _vp), ("stage_begin", _vp), ("local_index", _vp),
+        ("groups", _i64), ("group_patches", _i64), ("max_stage", _i64),
+    ]
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -156,6 +166,9 @@ def load() -> ctypes.CDLL:
         lib.intp_device_info.restype = _i32
         lib.svit_gather_patches.argtypes = [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp]
         lib.svit_gather_patches.restype = _i32
+        lib.svit_gather_patches_staged.argtypes = [_vp, _i64, _i64, ctypes.POINTER(SvitGatherPlan), _vp, _i64, _i64,
+                                                   _vp, _vp]
+        lib.svit_gather_patches_staged.restype = _i32
         lib.svit_embed_post.argtypes = [ctypes.POINTER(SvitEmbedArgs), _vp]
         lib.svit_embed_post.restype = _i32
         lib.svit_add_layernorm.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, ctypes.c_float, _i64, _i64, _vp, _i64, _vp]

@@ -39,6 +39,78 @@ __global__ void __launch_bounds__(256) gather_patches_kernel(const float* __rest
   }
 }
 
+// Staged gather: one CTA per (image, patch group).  Phase 1 copies the
+// group's distinct 16-byte image units (sorted, so consecutive threads read
+// runs of consecutive addresses) into shared memory with cp.async; phase 2
+// writes the group's rows, each thread 8 consecutive features (16 bytes),
+// from shared memory.  Several CTAs per SM overlap one's copies with
+// another's writes: the kernel is latency-bound, so it is compiled for 8 CTAs
+// per SM (32 registers) and groups should stay under 28 KB of shared memory.
+constexpr int kStagedThreads = 256;
+
+__global__ void __launch_bounds__(kStagedThreads, 8) gather_patches_staged_kernel(
+    const float* __restrict__ image, int64_t image_elems, const int32_t* __restrict__ stage_offset,
+    const int32_t* __restrict__ stage_begin, const int16_t* __restrict__ local_index,
+    const float* __restrict__ weight, int groups, int group_patches, int patches, int features,
+    uint4* __restrict__ out) {
+  extern __shared__ __align__(16) float staged[];
+  const int g = static_cast<int>(blockIdx.x % static_cast<unsigned>(groups));
+  const int64_t b = blockIdx.x / static_cast<unsigned>(groups);
+  const float4* img = reinterpret_cast<const float4*>(image + b * image_elems);
+  const int s0 = __ldg(stage_begin + g), count = __ldg(stage_begin + g + 1) - s0;
+  const uint32_t staged_base = smem_u32(staged);
+  // Offsets in batches of kStageBatch per thread: the batch's loads are all in
+  // flight before its copies are issued (one L2 round trip per batch).
+  constexpr int kStageBatch = 8;
+  for (int k0 = threadIdx.x; k0 < count; k0 += kStageBatch * kStagedThreads) {
+    int off[kStageBatch];
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int k = k0 + u * kStagedThreads;
+      off[u] = k < count ? __ldg(stage_offset + s0 + k) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int k = k0 + u * kStagedThreads;
+      if (k < count)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(staged_base + 16u * k), "l"(img + off[u])
+                     : "memory");
+    }
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+
+  const int n0 = g * group_patches;
+  const int rows = min(group_patches, patches - n0);
+  const int chunks = features / 8;
+  const uint4* idx = reinterpret_cast<const uint4*>(local_index + static_cast<int64_t>(n0) * features);
+  uint4* dst = out + (b * patches + n0) * chunks;
+  // Each thread keeps one 8-feature chunk (its weights in registers) for all
+  // the group's rows; kRowBatch rows' index words are loaded first.
+  constexpr int kRowBatch = 2;
+  for (int c = threadIdx.x; c < chunks; c += kStagedThreads) {
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c);
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c + 1);
+    for (int r0 = 0; r0 < rows; r0 += kRowBatch) {
+      uint4 li[kRowBatch];
+#pragma unroll
+      for (int u = 0; u < kRowBatch; ++u)
+        li[u] = r0 + u < rows ? __ldg(idx + (r0 + u) * chunks + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < kRowBatch; ++u) {
+        if (r0 + u < rows) {
+          const float v0 = staged[li[u].x & 0xffffu] * w0.x, v1 = staged[li[u].x >> 16] * w0.y;
+          const float v2 = staged[li[u].y & 0xffffu] * w0.z, v3 = staged[li[u].y >> 16] * w0.w;
+          const float v4 = staged[li[u].z & 0xffffu] * w1.x, v5 = staged[li[u].z >> 16] * w1.y;
+          const float v6 = staged[li[u].w & 0xffffu] * w1.z, v7 = staged[li[u].w >> 16] * w1.w;
+          dst[(r0 + u) * chunks + c] =
+              make_uint4(pack_bf16x2(v0, v1), pack_bf16x2(v2, v3), pack_bf16x2(v4, v5), pack_bf16x2(v6, v7));
+        }
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ post-GEMM
 // Geometry fixed at compile time: D directions, LP = supports x D Look poses.
 constexpr int kPostTokens = 32;    // patches per CTA
@@ -258,6 +330,35 @@ extern "C" INTP_API intp_status svit_gather_patches(const float* image, int64_t 
   const int64_t rows = batch * patches;
   gather_patches_kernel<<<grid_for(rows * (features / 8), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       image, image_elems, pixel_index, weight, patches, features, rows, static_cast<uint4*>(out));
+  return cudaGetLastError() == cudaSuccess ? INTP_OK : INTP_ERR_LAUNCH;
+}
+
+extern "C" INTP_API intp_status svit_gather_patches_staged(const float* image, int64_t batch, int64_t image_elems,
+                                                           const svit_gather_plan* plan, const float* weight,
+                                                           int64_t patches, int64_t features, void* out,
+                                                           void* stream) {
+  if (batch < 0 || patches < 0 || features < 0 || image_elems < 0 || !plan) return INTP_ERR_ARGUMENT;
+  if (batch == 0 || patches == 0 || features == 0) return INTP_OK;
+  if (!image || !weight || !out || !plan->stage_offset || !plan->stage_begin || !plan->local_index)
+    return INTP_ERR_ARGUMENT;
+  if (plan->group_patches <= 0 || plan->groups != (patches + plan->group_patches - 1) / plan->group_patches ||
+      plan->max_stage < 0)
+    return INTP_ERR_ARGUMENT;
+  if (features % 8 || image_elems % 4 || !aligned(image, 16) || !aligned(plan->local_index, 16) ||
+      !aligned(weight, 16) || !aligned(out, 16))
+    return INTP_ERR_LAYOUT;
+  constexpr int64_t kMaxShared = 227 * 1024;
+  const int64_t smem = plan->max_stage * static_cast<int64_t>(sizeof(float4));
+  if (smem > kMaxShared || patches > INT32_MAX / features || batch * plan->groups > INT32_MAX)
+    return INTP_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(gather_patches_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return INTP_ERR_LAUNCH;
+  gather_patches_staged_kernel<<<static_cast<unsigned>(batch * plan->groups), kStagedThreads, smem,
+                                 static_cast<cudaStream_t>(stream)>>>(
+      image, image_elems, plan->stage_offset, plan->stage_begin, plan->local_index, weight,
+      static_cast<int>(plan->groups), static_cast<int>(plan->group_patches), static_cast<int>(patches),
+      static_cast<int>(features), static_cast<uint4*>(out));
   return cudaGetLastError() == cudaSuccess ? INTP_OK : INTP_ERR_LAUNCH;
 }
 

@@ -52,8 +52,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .look_attention import LookSlotFields, LookSlots, look_attention_forward
-from .share_vit_ops import (add_layernorm, embed_post, gather_patches, linear_bias, linear_gelu,
-                            linear_residual_layernorm)
+from .share_vit_ops import (GatherPlan, add_layernorm, embed_post, gather_patches, gather_plan, linear_bias,
+                            linear_gelu, linear_residual_layernorm)
 
 IMAGE_SIZE = 224
 IN_CHANS = 3
@@ -338,6 +338,14 @@ class ShareViTHalf6d3r(nn.Module):
                 weight_parts.append(getattr(self, f"cover_{i}"))
         self.register_buffer("pixel_index", torch.cat(index_parts, dim=1).to(torch.int32).contiguous(), persistent=False)
         self.register_buffer("pixel_weight", torch.cat(weight_parts).float().contiguous(), persistent=False)
+        # Shared-memory plan of the same gather: groups of 6 consecutive patches
+        # (part of a column strip of the hex lattice, at most 1740 16-byte units:
+        # 27.2 KB of shared memory, 8 CTAs per SM).
+        plan = gather_plan(self.pixel_index, group_patches=6)
+        self.register_buffer("gather_stage_offset", plan.stage_offset, persistent=False)
+        self.register_buffer("gather_stage_begin", plan.stage_begin, persistent=False)
+        self.register_buffer("gather_local_index", plan.local_index, persistent=False)
+        self._gather_plan_sizes = (plan.group_patches, plan.max_stage, plan.max_offset)
         theta = torch.arange(DIRECTIONS) * (2 * math.pi / GLOBAL_DIRECTIONS)
         self.register_buffer("direction_coefficients", torch.stack((torch.cos(theta), torch.sin(theta)), -1),
                              persistent=False)
@@ -484,7 +492,9 @@ class ShareViTHalf6d3r(nn.Module):
         batch, n = image.shape[0], self.num_patches
         image = image.float().contiguous()
         w, fields = self._fused_embed_weights(image.device)
-        patches = gather_patches(image, self.pixel_index, self.pixel_weight)
+        plan = GatherPlan(self.gather_stage_offset, self.gather_stage_begin, self.gather_local_index,
+                          *self._gather_plan_sizes)
+        patches = gather_patches(image, self.pixel_index, self.pixel_weight, plan=plan)
         resp = patches @ w.t()
         x = torch.empty(batch, n + 1, EMBED_DIM, dtype=torch.float32, device=image.device)
         values = look_pose = None

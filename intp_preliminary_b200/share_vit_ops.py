@@ -9,6 +9,7 @@ CPU tensors, wrong dtypes or layouts raise ``ValueError``.
 from __future__ import annotations
 
 import ctypes
+from typing import NamedTuple
 
 import torch
 
@@ -28,12 +29,62 @@ def _require(cond: bool, message: str) -> None:
         raise ValueError(message)
 
 
+class GatherPlan(NamedTuple):
+    """Shared-memory plan of the patch gather (``svit_gather_plan``): patches in
+    groups of ``group_patches``; each group's distinct 16-byte image units (4
+    pixels, offset // 4), sorted, in ``stage_offset[stage_begin[g]:stage_begin[g + 1]]``
+    (int32); ``local_index`` (N, F) int16, the pixel's float position among its
+    group's staged units (4 * unit rank + offset % 4)."""
+
+    stage_offset: torch.Tensor
+    stage_begin: torch.Tensor
+    local_index: torch.Tensor
+    group_patches: int
+    max_stage: int
+    max_offset: int
+
+    def to(self, device: torch.device | str) -> "GatherPlan":
+        return self._replace(stage_offset=self.stage_offset.to(device), stage_begin=self.stage_begin.to(device),
+                             local_index=self.local_index.to(device))
+
+
+# int16 float positions: at most 8191 units of 16 bytes (128 KB of shared memory).
+_MAX_STAGE = 8191
+
+
+def gather_plan(pixel_index: torch.Tensor, group_patches: int = 6) -> GatherPlan:
+    """Build the staged gather's plan from ``pixel_index`` (N, F) int32 (host
+    work, once per patch geometry).  The result lives on ``pixel_index``'s device."""
+    _require(pixel_index.dtype == torch.int32 and pixel_index.ndim == 2, "pixel_index must be an (N, F) int32 tensor")
+    _require(group_patches > 0, "group_patches must be positive")
+    index = pixel_index.detach().cpu().long()
+    patches, features = index.shape
+    _require(features % 8 == 0, "features must be a multiple of 8")
+    _require(patches == 0 or int(index.min()) >= 0, "pixel_index must be non-negative")
+    offsets, begin, local = [], [0], torch.empty(patches, features, dtype=torch.int16)
+    for n0 in range(0, patches, group_patches):
+        rows = index[n0:n0 + group_patches]
+        units, rank = torch.unique(rows // 4, sorted=True, return_inverse=True)
+        _require(units.numel() <= _MAX_STAGE, f"a group of {group_patches} patches reads {units.numel()} "
+                 f"16-byte units (at most {_MAX_STAGE}); use smaller groups")
+        offsets.append(units.to(torch.int32))
+        begin.append(begin[-1] + units.numel())
+        local[n0:n0 + group_patches] = (4 * rank + rows % 4).to(torch.int16)
+    counts = [b - a for a, b in zip(begin[:-1], begin[1:])]
+    stage_offset = torch.cat(offsets) if offsets else torch.zeros(0, dtype=torch.int32)
+    device = pixel_index.device
+    return GatherPlan(stage_offset.to(device), torch.tensor(begin, dtype=torch.int32, device=device),
+                      local.to(device), group_patches, max(counts, default=0),
+                      int(index.max()) if patches else -1)
+
+
 def gather_patches(image: torch.Tensor, pixel_index: torch.Tensor, weight: torch.Tensor,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
+                   out: torch.Tensor | None = None, plan: GatherPlan | None = None) -> torch.Tensor:
     """``out[b*N + n, f] = bf16(image[b].flatten()[pixel_index[n, f]] * weight[f])``.
 
     image (B, C, H, W) float32 contiguous CUDA; pixel_index (N, F) int32;
-    weight (F,) float32.  Returns (B*N, F) bf16."""
+    weight (F,) float32.  Returns (B*N, F) bf16.  With ``plan`` (from
+    ``gather_plan(pixel_index)``) the gather runs through shared memory."""
     _require(image.is_cuda and image.dtype == torch.float32 and image.is_contiguous(),
              "image must be a contiguous float32 CUDA tensor")
     _require(pixel_index.dtype == torch.int32 and pixel_index.ndim == 2 and pixel_index.is_contiguous(),
@@ -47,9 +98,24 @@ def gather_patches(image: torch.Tensor, pixel_index: torch.Tensor, weight: torch
         out = torch.empty((batch * patches, features), dtype=torch.bfloat16, device=image.device)
     _require(out.shape == (batch * patches, features) and out.dtype == torch.bfloat16 and out.is_contiguous(),
              "out must be a contiguous (B*N, F) bf16 tensor")
-    status = _lib.load().svit_gather_patches(
-        _ptr(image), batch, image[0].numel() if batch else 0, _ptr(pixel_index), _ptr(weight), patches, features,
-        _ptr(out), _stream(image.device))
+    image_elems = image[0].numel() if batch else 0
+    if plan is None:
+        status = _lib.load().svit_gather_patches(
+            _ptr(image), batch, image_elems, _ptr(pixel_index), _ptr(weight), patches, features,
+            _ptr(out), _stream(image.device))
+    else:
+        _require(plan.local_index.shape == (patches, features) and plan.local_index.dtype == torch.int16
+                 and plan.local_index.is_contiguous(), "plan does not match pixel_index")
+        _require(all(t.device == image.device for t in (plan.stage_offset, plan.stage_begin, plan.local_index)),
+                 "plan must be on the image's device")
+        _require(batch == 0 or (plan.max_offset < image_elems and image_elems % 4 == 0),
+                 "plan reads beyond one image, or images are not whole 16-byte units")
+        groups = plan.stage_begin.numel() - 1
+        args = _lib.SvitGatherPlan(_ptr(plan.stage_offset).value, _ptr(plan.stage_begin).value,
+                                   _ptr(plan.local_index).value, groups, plan.group_patches, plan.max_stage)
+        status = _lib.load().svit_gather_patches_staged(
+            _ptr(image), batch, image_elems, ctypes.byref(args), _ptr(weight), patches, features, _ptr(out),
+            _stream(image.device))
     _lib.check(status, "hex patch gather")
     return out
 
@@ -236,6 +302,45 @@ def _time_block_linears(batch: int = 256, steps: int = 20) -> dict[str, float]:
     return result
 
 
+def _time_patch_gather(batch: int = 256, steps: int = 20) -> dict[str, float]:
+    """The half6d3r patch gather (batch seeded 224 x 224 x 3 images, the model's
+    (195, 1680) pixel table), direct and staged: 3 warm-up calls each (the
+    staged launches a profiler skips with ``-s 3``), then ``steps`` calls each,
+    every call timed alone with CUDA events after a 256 MB write that flushes
+    the L2.  Returns the median microseconds per call."""
+    from .share_vit import ShareViTHalf6d3r
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = ShareViTHalf6d3r().to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    images = torch.randn(batch, 3, 224, 224, device=dev, generator=g)
+    out = torch.empty(batch * model.num_patches, model.pixel_index.shape[1], dtype=torch.bfloat16, device=dev)
+    plan = GatherPlan(model.gather_stage_offset, model.gather_stage_begin, model.gather_local_index,
+                      *model._gather_plan_sizes)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    calls = {
+        "staged (shared-memory plan)": lambda: gather_patches(images, model.pixel_index, model.pixel_weight, out,
+                                                              plan=plan),
+        "direct": lambda: gather_patches(images, model.pixel_index, model.pixel_weight, out),
+    }
+    result = {}
+    for name, fn in calls.items():
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(steps):
+            flush.fill_(1)
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            stop.record()
+            torch.cuda.synchronize()
+            times.append(start.elapsed_time(stop) * 1000.0)
+        result[name] = sorted(times)[len(times) // 2]
+    return result
+
+
 if __name__ == "__main__":
-    for name, us in _time_block_linears().items():
+    import sys
+    runner = _time_patch_gather if sys.argv[1:] == ["gather"] else _time_block_linears
+    for name, us in runner().items():
         print(f"{name}: {us:.1f} us")

@@ -39,6 +39,9 @@ def test_svit_struct_layout_matches_header_field_order():
     body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
     names = re.findall(r"(\w+)\s*[;,]", body)
     assert names == [f[0] for f in _lib.SvitEmbedArgs._fields_]
+    body = text[text.index("typedef struct svit_gather_plan"):text.index("} svit_gather_plan;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    assert re.findall(r"(\w+)\s*[;,]", body) == [f[0] for f in _lib.SvitGatherPlan._fields_]
 
 
 def test_svit_host_side_argument_checks():
@@ -46,6 +49,22 @@ def test_svit_host_side_argument_checks():
     # zero-sized work is a no-op; bad sizes are rejected before any launch
     assert lib.svit_gather_patches(None, 0, 0, None, None, 0, 0, None, None) == _lib.INTP_OK
     assert lib.svit_gather_patches(None, -1, 0, None, None, 1, 8, None, None) == _lib.INTP_ERR_ARGUMENT
+    plan = _lib.SvitGatherPlan(16, 16, 16, 2, 8, 100)
+    assert lib.svit_gather_patches_staged(None, 0, 0, ctypes.byref(plan), None, 0, 0, None, None) == _lib.INTP_OK
+    assert lib.svit_gather_patches_staged(None, 1, 10, None, None, 9, 8, None, None) == _lib.INTP_ERR_ARGUMENT
+    fake = 1 << 20  # never dereferenced: every case below is rejected before a launch
+    plan.groups = 3  # 9 patches in groups of 8 are 2 groups
+    assert lib.svit_gather_patches_staged(fake, 1, 10, ctypes.byref(plan), fake, 9, 8, fake, None) == \
+        _lib.INTP_ERR_ARGUMENT
+    plan.groups, plan.local_index = 2, 18  # local_index not 16-byte aligned
+    assert lib.svit_gather_patches_staged(fake, 1, 10, ctypes.byref(plan), fake, 9, 8, fake, None) == \
+        _lib.INTP_ERR_LAYOUT
+    plan.local_index = 16  # images of 10 floats are not whole 16-byte units
+    assert lib.svit_gather_patches_staged(fake, 1, 10, ctypes.byref(plan), fake, 9, 8, fake, None) == \
+        _lib.INTP_ERR_LAYOUT
+    plan.max_stage = 15000  # 240 KB of shared memory
+    assert lib.svit_gather_patches_staged(fake, 1, 12, ctypes.byref(plan), fake, 9, 8, fake, None) == \
+        _lib.INTP_ERR_UNSUPPORTED
     assert lib.svit_add_layernorm(None, 0, None, 0, None, None, 1e-6, 0, 192, None, 0, None) == _lib.INTP_OK
     assert lib.svit_add_layernorm(None, 0, None, 0, None, None, 1e-6, 3, 192, None, 0, None) == _lib.INTP_ERR_ARGUMENT
     a = _lib.SvitEmbedArgs()

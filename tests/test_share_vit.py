@@ -94,6 +94,39 @@ def test_fused_embed_weight_matrix_layout(model):
     assert fields.shape == (36, 12, 68)
 
 
+def test_gather_plan_reproduces_pixel_index(model):
+    """Each group's sorted distinct 16-byte units, addressed by local_index,
+    give back pixel_index; the model's groups fit the kernel's shared memory."""
+    from intp_preliminary_b200.share_vit_ops import gather_plan
+    for group in (1, 4, 13, 26):
+        plan = gather_plan(model.pixel_index, group)
+        index = model.pixel_index.long()
+        begin = plan.stage_begin.tolist()
+        assert len(begin) == -(-index.shape[0] // group) + 1 and begin[0] == 0
+        for g in range(len(begin) - 1):
+            units = plan.stage_offset[begin[g]:begin[g + 1]].long()
+            assert torch.all(units[1:] > units[:-1])
+            rows = slice(g * group, (g + 1) * group)
+            local = plan.local_index[rows].long()
+            assert torch.equal(4 * units[local // 4] + local % 4, index[rows])
+        assert plan.max_stage == max(b - a for a, b in zip(begin[:-1], begin[1:]))
+        assert plan.max_offset == int(index.max())
+    assert model.gather_stage_begin.numel() - 1 == -(-model.num_patches // model._gather_plan_sizes[0])
+    assert model._gather_plan_sizes[1] * 16 * 8 <= 228 * 1024  # 8 CTAs per SM
+
+
+def test_gather_plan_rejects_bad_tables():
+    from intp_preliminary_b200.share_vit_ops import gather_plan
+    with pytest.raises(ValueError):
+        gather_plan(torch.full((2, 8), -1, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        gather_plan(torch.zeros(2, 6, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        gather_plan(torch.zeros(2, 8, dtype=torch.int32), group_patches=0)
+    with pytest.raises(ValueError):
+        gather_plan(torch.arange(40000 * 8, dtype=torch.int32).reshape(40000, 8), group_patches=5000)  # 10000 units
+
+
 def test_fused_op_wrappers_reject_cpu_tensors():
     from intp_preliminary_b200 import share_vit_ops as ops
     with pytest.raises(ValueError):

@@ -25,6 +25,39 @@ def test_gather_patches_matches_reflect_gather(model, cuda_device):
     assert torch.equal(got, ref.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("group_patches", [1, 5, 8, 13, 26])
+def test_staged_gather_equals_direct_gather(model, cuda_device, group_patches):
+    """The shared-memory gather is bit-exact with the direct one on the model's
+    geometry, for any grouping (partial last groups, up to 26 patches per group)."""
+    images = torch.randn(5, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(3))
+    plan = ops.gather_plan(model.pixel_index, group_patches)
+    got = ops.gather_patches(images, model.pixel_index, model.pixel_weight, plan=plan)
+    assert torch.equal(got, ops.gather_patches(images, model.pixel_index, model.pixel_weight))
+
+
+def test_staged_gather_random_geometry(cuda_device):
+    """Arbitrary offsets (repeats, unsorted, touching the image's last element)."""
+    g = torch.Generator().manual_seed(4)
+    images = torch.randn(3, 2, 9, 12, generator=g).to(cuda_device)
+    index = torch.randint(0, 2 * 9 * 12, (37, 64), generator=g, dtype=torch.int32)
+    index[5, 7] = 2 * 9 * 12 - 1
+    weight = torch.randn(64, generator=g)
+    index, weight = index.to(cuda_device), weight.to(cuda_device)
+    ref = (images.reshape(3, -1)[:, index.long()] * weight).reshape(3 * 37, 64).to(torch.bfloat16)
+    for group in (1, 4, 37):
+        got = ops.gather_patches(images, index, weight, plan=ops.gather_plan(index, group))
+        assert torch.equal(got, ref)
+
+
+def test_model_embed_uses_staged_gather(model, cuda_device):
+    """The model's registered plan is the one gather_plan builds."""
+    plan = ops.gather_plan(model.pixel_index, model._gather_plan_sizes[0])
+    assert (plan.group_patches, plan.max_stage, plan.max_offset) == model._gather_plan_sizes
+    assert torch.equal(model.gather_stage_offset, plan.stage_offset)
+    assert torch.equal(model.gather_local_index, plan.local_index)
+    assert model.gather_stage_offset.device == model.pixel_index.device
+
+
 @pytest.mark.parametrize("rows,dim", [(1, 192), (37, 192), (50432 // 16, 192), (9, 64), (5, 512)])
 def test_add_layernorm_matches_torch(cuda_device, rows, dim):
     g = torch.Generator(cuda_device).manual_seed(rows)
