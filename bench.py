@@ -9,7 +9,9 @@ in place inside that forward (``roofline``) and BASELINE config 4 (B64 H6
 N1025 D64 bf16) timed on its own (``look_attention_cfg4``).
 
 Other workloads: ``look_cfg4`` / ``look_cfg1`` (one Look-attention forward per
-step, TFLOP/s) and ``negative_l1`` (M=256*196, P=576, F=1728 fp32).
+step, TFLOP/s), ``negative_l1`` (M=256*196, P=576, F=1728 fp32) and
+``dense_look_grid`` (dense Look-grid sampling, B256 H3 on the 14x14 lattice,
+fp32 grids -> the (B, H, 196, 196) bias, GB/s; its backward timed alongside).
 
 Contract: ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``;
 for N > 1 launch one process per GPU with torchrun.  Timing: CUDA events on the
@@ -341,6 +343,86 @@ class NegativeL1Workload:
             f"{rows} rows of negative_l1, -cdist p=1"
 
 
+class DenseLookGridWorkload:
+    unit = "GB/s"
+    metric = "dense Look-grid sampling bias throughput (algorithmic bytes / s)"
+    dtype = torch.float32
+    name = "dense_look_grid"
+
+    def __init__(self, device: torch.device, seed: int, world: int = 1):
+        from intp_preliminary_b200 import hexgrid, look_sampling_tables
+
+        coords = torch.from_numpy(hexgrid.offset_row_lattice(14, 14)).float()
+        self.tables = [t.to(device) for t in look_sampling_tables(coords).values()]
+        self.batch, self.queries, self.heads, self.world = 256, coords.shape[0], 3, world
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.grid = torch.randn(self.batch, self.queries, self.heads, 4, 12, device=device, generator=g)
+        self.out = torch.empty(self.batch, self.heads, self.queries, self.queries, device=device)
+        self.grad_out = torch.randn(self.out.shape, device=device, generator=g)
+        self.device = device
+
+    @property
+    def bytes(self) -> float:  # grid read + bias written + the seven (Q, Q) tables read once
+        q = self.queries
+        return 4.0 * (self.grid.numel() + self.out.numel()) + q * q * (4 * 8 + 2 * 4 + 1)
+
+    @property
+    def backward_bytes(self) -> float:  # grad_out read + grad_grid written + tables
+        q = self.queries
+        return 4.0 * (self.grad_out.numel() + self.grid.numel()) + q * q * (4 * 8 + 2 * 4 + 1)
+
+    @property
+    def units_per_step(self) -> float:
+        return self.bytes * self.world / 1e9
+
+    @property
+    def config(self) -> dict:
+        return {"workload": f"dense_look_grid: grid ({self.batch}, {self.queries}, {self.heads}, 4, 12) fp32 -> "
+                            f"bias ({self.batch}, {self.heads}, {self.queries}, {self.queries}) fp32, "
+                            "14x14 hex lattice tables", "batch": self.batch, "heads": self.heads,
+                "queries": self.queries}
+
+    def step(self):
+        from intp_preliminary_b200 import dense_look_grid_forward
+
+        dense_look_grid_forward(self.grid, *self.tables, out=self.out)
+
+    def backward_step(self):
+        from intp_preliminary_b200 import dense_look_grid_backward
+
+        dense_look_grid_backward(self.grad_out, *self.tables, grid_shape=self.grid.shape)
+
+    def e2e_inputs(self):
+        return [self.grid.cpu().pin_memory()]
+
+    def e2e_output(self):
+        return torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+
+    def e2e_step(self, host_inputs, host_out):
+        from intp_preliminary_b200 import dense_look_grid_sample
+
+        grid = host_inputs[0].to(self.device, non_blocking=True)
+        host_out.copy_(dense_look_grid_sample(grid, *self.tables), non_blocking=True)
+
+    def cpu_reference(self):
+        from oracle.dense_look_grid import dense_look_grid_np
+
+        batch = 8
+        grid = self.grid[:batch].cpu().numpy()
+        tables = {name: t.cpu().numpy() for name, t in zip(
+            ("radial0", "radial1", "angular0", "angular1", "radial_fraction", "angular_fraction", "valid"),
+            self.tables)}
+        dense_look_grid_np(grid, tables)
+        times, t_end = [], time.perf_counter() + 10.0
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            dense_look_grid_np(grid, tables)
+            times.append(time.perf_counter() - t0)
+        sample_bytes = self.bytes * batch / self.batch
+        return sample_bytes / statistics.median(times) / 1e9, \
+            f"{batch} of {self.batch} images of dense_look_grid through the oracle sampler (numpy float64)"
+
+
 # --------------------------------------------------------------------------- timing
 def _model_attention_ms(work, args, ctx, flush: torch.Tensor) -> float:
     """Mean device ms of one Look-attention launch on the model's own inputs:
@@ -413,6 +495,8 @@ def run_ours(args) -> None:
         work = ModelWorkload(ctx, args.batch, seed=1234)
     elif args.workload.startswith("look"):
         work = LookWorkload(args.workload, device, seed=1234 + ctx.rank, world=ctx.world)
+    elif args.workload == "dense_look_grid":
+        work = DenseLookGridWorkload(device, seed=1234 + ctx.rank, world=ctx.world)
     else:
         work = NegativeL1Workload(device, seed=1234 + ctx.rank, world=ctx.world)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
@@ -456,6 +540,17 @@ def run_ours(args) -> None:
                                   CFG4_TRAFFIC_BYTES if work.name == "look_cfg4" else None,
                                   "sla_tc_kernel" if work.dtype != torch.float32 else "sla_simt_kernel",
                                   "one launch per timed step")
+        launches = args.steps
+    elif isinstance(work, DenseLookGridWorkload):
+        gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "dlg_forward_kernel",
+                    "peak_source": f"{peaks['source']} HBM copy bandwidth"}
+        bwd_times = _timed_steps(work.backward_step, args.steps, args.warmup, ctx, flush)
+        bwd_ms = max_over_ranks(statistics.mean(bwd_times), ctx)
+        bwd_gbs = work.backward_bytes / (bwd_ms * 1e-3) / 1e9
+        extra["backward"] = {"kernel": "dlg_backward_kernel", "ms": round(bwd_ms, 4), "achieved_gbs": round(bwd_gbs, 1),
+                             "frac": round(bwd_gbs / peaks["hbm_gbs"], 4)}
         launches = args.steps
     else:
         gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
@@ -589,7 +684,8 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["model", "look_cfg4", "look_cfg1", "negative_l1"], default="model")
+    parser.add_argument("--workload", choices=["model", "look_cfg4", "look_cfg1", "negative_l1", "dense_look_grid"],
+                        default="model")
     parser.add_argument("--batch", type=int, default=256, help="images per GPU (model workload)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()

@@ -168,6 +168,52 @@ INTP_API intp_status nl1_forward(const float* x, const float* w, float* out,
 INTP_API intp_status nl1_backward(const float* x, const float* w, const float* grad_out, float* grad_x,
                          float* grad_w, int64_t rows, int64_t protos, int64_t features, void* stream);
 
+/* Dense Look-grid sampling: out[b,h,q,k] = sum over the four corners j of
+ * grid[b,q,h,r_j,a_j] * w_j, with corners (r0,a0), (r0,a1), (r1,a0), (r1,a1)
+ * and weights (1-rw)(1-aw), (1-rw)aw, rw(1-aw), rw aw taken from the (Q, Q)
+ * sampling tables at (q, k); 0 where valid[q,k] is false (a corner index
+ * outside 0..3 / 0..11 also counts 0).  Replaces the launch of
+ * `_dense_look_grid_forward` in `_DenseLookGridSample.forward`
+ * (layers/triton_dense_look_grid.py:114-150), reached through
+ * `dense_look_grid_sample` (:184-202).
+ *   grid  : (batch, queries, heads, 4, 12), dtype `dtype`, any strides
+ *   tables: radial0, radial1, angular0, angular1 int64; radial_fraction,
+ *           angular_fraction float32; valid bool (one byte); each (queries,
+ *           queries) with its own (q, k) element strides, in that order
+ *   out   : (batch, heads, queries, queries), dtype `dtype`, any strides
+ * Arithmetic in float32, one rounding to `dtype` at the store.              */
+typedef struct dlg_args {
+  int64_t batch, queries, heads;
+  int32_t dtype;                 /* INTP_F32 / INTP_F16 / INTP_BF16 (grid, out) */
+  const void* grid;  int64_t grid_stride[5];
+  const int64_t* radial0;
+  const int64_t* radial1;
+  const int64_t* angular0;
+  const int64_t* angular1;
+  const float* radial_fraction;
+  const float* angular_fraction;
+  const uint8_t* valid;
+  int64_t table_stride[7][2];    /* (q, k) strides of the seven tables above  */
+  void* out;         int64_t out_stride[4];
+} dlg_args;
+
+typedef struct dlg_grad_strides {
+  int64_t stride[4];             /* (batch, heads, queries, keys) of grad_out */
+} dlg_grad_strides;
+
+INTP_API intp_status dlg_forward(const dlg_args* args, void* stream);
+
+/* Gradient of dlg_forward with respect to the grid (the reference's
+ * scatter_add backward, layers/triton_dense_look_grid.py:152-181):
+ * grad_grid[b,q,h,r,a] = sum over (k, corner j) with (r_j, a_j) = (r, a) of
+ * grad_out[b,h,q,k] * w_j(q, k).  grad_out has dtype args->dtype and the
+ * strides `grad_strides`; grad_grid is written contiguous (batch, queries,
+ * heads, 4, 12) in args->dtype.  Each cell is summed in float32 in a fixed
+ * (key, corner) order, so the result is deterministic.  args->grid and
+ * args->out are not used.  queries <= 1024.                                 */
+INTP_API intp_status dlg_backward(const dlg_args* args, const void* grad_out, const dlg_grad_strides* grad_strides,
+                                  void* grad_grid, void* stream);
+
 /* Copies the device status word written by bounded waits to the host
  * (synchronous on `stream`) and clears it.  *code = 0 when no wait failed.  */
 INTP_API intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream);

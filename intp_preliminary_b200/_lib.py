@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "nl1_backward",
     "sla_read_status",
     "sla_forward_noalloc",
+    "dlg_forward",
+    "dlg_backward",
     "intp_device_info",
     "intp_abi_version",
     "intp_status_string",
@@ -115,6 +117,26 @@ class SvitEmbedArgs(ctypes.Structure):
     ]
 
 
+class DlgArgs(ctypes.Structure):
+    """Mirror of ``dlg_args`` (include/intp_b200.h)."""
+
+    _fields_ = [
+        ("batch", _i64), ("queries", _i64), ("heads", _i64),
+        ("dtype", _i32),
+        ("grid", _vp), ("grid_stride", _i64 * 5),
+        ("radial0", _vp), ("radial1", _vp), ("angular0", _vp), ("angular1", _vp),
+        ("radial_fraction", _vp), ("angular_fraction", _vp), ("valid", _vp),
+        ("table_stride", (_i64 * 2) * 7),
+        ("out", _vp), ("out_stride", _Stride),
+    ]
+
+
+class DlgGradStrides(ctypes.Structure):
+    """Mirror of ``dlg_grad_strides`` (include/intp_b200.h)."""
+
+    _fields_ = [("stride", _Stride)]
+
+
 class SvitGatherPlan(ctypes.Structure):
     """Mirror of ``svit_gather_plan`` (include/intp_share_vit.h)."""
 
@@ -160,6 +182,10 @@ def load() -> ctypes.CDLL:
         lib.nl1_forward.restype = _i32
         lib.sla_forward_noalloc.argtypes = [ctypes.POINTER(SlaForwardArgs), _vp, _vp]
         lib.sla_forward_noalloc.restype = _i32
+        lib.dlg_forward.argtypes = [ctypes.POINTER(DlgArgs), _vp]
+        lib.dlg_forward.restype = _i32
+        lib.dlg_backward.argtypes = [ctypes.POINTER(DlgArgs), _vp, ctypes.POINTER(DlgGradStrides), _vp, _vp]
+        lib.dlg_backward.restype = _i32
         lib.sla_read_status.argtypes = [_vp, ctypes.POINTER(_i32), _vp]
         lib.sla_read_status.restype = _i32
         lib.intp_device_info.argtypes = [ctypes.POINTER(_i32)] * 3

@@ -22,6 +22,12 @@ reference checkout is available, passed as --reference, default
       seeded images, with the weights of ``ShareViTHalf6d3r.init_weights(seed=0,
       look_grid_std=0.5)`` loaded into it: logits, CLS features, the first 8
       patch tokens and Look pose weights.
+  dense_look_grid_reference.npz
+      ``reference_dense_look_grid_sample`` (layers/triton_dense_look_grid.py:19-49)
+      and its autograd gradient on seeded grids (fp32, and bf16-rounded values),
+      with the sampling tables that the reference's
+      ``TwoRingCircularLookMatcher._register_look_sampling_buffers``
+      (layers/two_ring_circular_look.py:124-152) registers for a 6 x 7 hex lattice.
 
 The slot tables of the synthetic configurations come from the scalar oracle
 restatement (oracle/hex_lattice.py); the reference has no code for that
@@ -29,7 +35,7 @@ binning (it is defined by the benchmark description), so the fixture pins the
 reference's attention math on those inputs and the product's table builder is
 checked against the oracle separately.
 
-Run: python tests/golden/make_golden.py [--reference PATH]
+Run: python tests/golden/make_golden.py [--reference PATH] [--only dense_look_grid]
 """
 
 from __future__ import annotations
@@ -82,12 +88,42 @@ def _synthetic_case(ref_fn, lattice, *, rows, cols, n_dir, n_rad, batch, heads, 
     }
 
 
+def _dense_look_grid() -> None:
+    from layers.triton_dense_look_grid import reference_dense_look_grid_sample as ref_sample
+    from layers.two_ring_circular_look import TwoRingCircularLookMatcher
+    from oracle import hex_lattice
+
+    coords = torch.tensor(np.asarray(hex_lattice.lattice_points(6, 7)), dtype=torch.float32)
+    holder = torch.nn.Module()
+    TwoRingCircularLookMatcher._register_look_sampling_buffers(holder, coords)
+    names = ("radial0", "radial1", "angular0", "angular1", "radial_fraction", "angular_fraction", "valid")
+    tables = [getattr(holder, f"look_{name}") for name in names]
+    g = torch.Generator().manual_seed(31)
+    batch, queries, heads = 2, coords.shape[0], 3
+    grid = torch.randn(batch, queries, heads, 4, 12, generator=g)
+    grad_out = torch.randn(batch, heads, queries, queries, generator=g)
+    out = {"coordinates": coords.numpy(), "grid": grid.numpy(), "grad_out": grad_out.numpy()}
+    for name, t in zip(names, tables):
+        out[name] = t.numpy()
+    for tag, values in (("", grid), ("_bf16", grid.to(torch.bfloat16).float())):
+        leaf = values.clone().requires_grad_(True)
+        bias = ref_sample(leaf, *tables)
+        bias.backward(grad_out)
+        out[f"bias{tag}"] = bias.detach().numpy()
+        out[f"grad_grid{tag}"] = leaf.grad.numpy()
+    np.savez_compressed(HERE / "dense_look_grid_reference.npz", **out)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--only", choices=("all", "dense_look_grid"), default="all")
     args = parser.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     sys.path.insert(0, str(REPO))
+    _dense_look_grid()
+    if args.only == "dense_look_grid":
+        return
     from layers.triton_structured_look_attention import reference_structured_look_attention as ref_attn
     from layers.triton_negative_l1 import negative_l1_distance as ref_nl1
     from utils.hex_graph import hex_relative_bins
