@@ -141,14 +141,17 @@ __global__ void __launch_bounds__(kThreads) dlg_forward_kernel(const dlg_args a)
 // corners are listed once per cell, in (key, corner) order, so each grid cell is
 // a short sum in a fixed order (deterministic, fp32), then grad_out rows are
 // staged kBwdSubRows at a time (kLoadBatch independent loads per thread in
-// flight) and each thread finishes whole cells.
+// flight); a warp sums one cell for 32 rows at once (lane = row) into a
+// shared tile that is written out coalesced.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) dlg_backward_kernel(const dlg_args a, const void* __restrict__ grad_out,
                                                                  dlg_grad_strides gs, void* __restrict__ grad_grid) {
   extern __shared__ __align__(16) float smem_bwd[];
   const int K = static_cast<int>(a.queries);
-  float* gsub = smem_bwd;                                   // [kBwdSubRows][K]
-  float* entry_w = gsub + kBwdSubRows * K;                  // [4K]
+  const int Kp = K | 1;                                     // odd row stride: lanes on rows hit distinct banks
+  float* gsub = smem_bwd;                                   // [kBwdSubRows][Kp]
+  float* out_s = gsub + kBwdSubRows * Kp;                   // [kBwdSubRows][kCells + 1]
+  float* entry_w = out_s + kBwdSubRows * (kCells + 1);      // [4K]
   int* entry_k = reinterpret_cast<int*>(entry_w + 4 * K);   // [4K]
   uint32_t* key_cells = reinterpret_cast<uint32_t*>(entry_k + 4 * K);  // [K] four cells, a byte each (255: none)
   float* key_w = reinterpret_cast<float*>(key_cells + K);   // [K][4]
@@ -242,10 +245,13 @@ __global__ void __launch_bounds__(kThreads) dlg_backward_kernel(const dlg_args a
     int rl = threadIdx.x / K, k = threadIdx.x % K;
     for (int i0 = threadIdx.x; i0 < total; i0 += kLoadBatch * kThreads) {
       float v[kLoadBatch];
+      int dst[kLoadBatch];
       int ru = rl, ku = k;
 #pragma unroll
       for (int u = 0; u < kLoadBatch; ++u) {
-        v[u] = i0 + u * kThreads < total ? to_f32(go[go_row[ru] + ku * gs.stride[3]]) : 0.f;
+        const bool in = i0 + u * kThreads < total;
+        v[u] = in ? to_f32(go[go_row[ru] + ku * gs.stride[3]]) : 0.f;
+        dst[u] = in ? ru * Kp + ku : -1;
         ru += step_r;
         ku += step_k;
         if (ku >= K) {
@@ -254,26 +260,34 @@ __global__ void __launch_bounds__(kThreads) dlg_backward_kernel(const dlg_args a
         }
       }
 #pragma unroll
-      for (int u = 0; u < kLoadBatch; ++u) {
-        const int i = i0 + u * kThreads;
-        if (i < total) gsub[i] = v[u];
-      }
+      for (int u = 0; u < kLoadBatch; ++u)
+        if (dst[u] >= 0) gsub[dst[u]] = v[u];
       rl = ru;
       k = ku;
     }
     __syncthreads();
+    // lane = row of the sub-chunk, warp w = cells w, w + 8, ...: every lane of a
+    // warp walks the same list (broadcast loads, no divergence)
+    {
+      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      const float* grow = gsub + lane * Kp;
+      for (int cell = warp; cell < kCells; cell += kThreads / 32) {
+        float s = 0.f;
+        for (int e = seg_begin[4 * cell]; e < seg_begin[4 * cell + 4]; ++e) s = fmaf(grow[entry_k[e]], entry_w[e], s);
+        out_s[lane * (kCells + 1) + cell] = s;
+      }
+    }
+    __syncthreads();
     for (int o = threadIdx.x; o < sub * kCells; o += kThreads) {
       const int orl = o / kCells, cell = o - orl * kCells;
-      const float* grow = gsub + orl * K;
-      float s = 0.f;
-      for (int e = seg_begin[4 * cell]; e < seg_begin[4 * cell + 4]; ++e) s = fmaf(grow[entry_k[e]], entry_w[e], s);
-      gg[gg_row[orl] + cell] = from_f32<T>(s);
+      gg[gg_row[orl] + cell] = from_f32<T>(out_s[orl * (kCells + 1) + cell]);
     }
   }
 }
 
 size_t backward_smem(int64_t keys) {
-  return static_cast<size_t>(kBwdSubRows * keys + 4 * keys + 4 * keys + keys + 4 * keys) * 4;
+  return static_cast<size_t>(kBwdSubRows * (keys | 1) + kBwdSubRows * (kCells + 1) + 4 * keys + 4 * keys + keys +
+                             4 * keys) * 4;
 }
 
 intp_status check_args(const dlg_args* a) {
