@@ -627,8 +627,30 @@ def run_reference(args) -> None:
         work = _CpuLook(args.workload)
         step, units, unit = work.step, work.sample_flops / 1e12, "TFLOP/s"
         metric, config, sample, dtype = LookWorkload.metric, work.config, work.sample, work.dtype_name
+    elif args.workload == "negative_l1":
+        from oracle.negative_l1 import negative_l1_torch
+
+        g = torch.Generator().manual_seed(1234)
+        rows, protos, features = 2048, 576, 1728
+        x, w = torch.randn(rows, features, generator=g), torch.randn(protos, features, generator=g) * 0.5
+        step = lambda: negative_l1_torch(x, w)  # noqa: E731
+        units, unit = 2.0 * rows * protos * features / 1e12, "TFLOP/s"
+        metric, dtype = NegativeL1Workload.metric, "f32"
+        config = {"workload": f"negative_l1: x ({256 * 196}, {features}) fp32 vs prototypes ({protos}, {features})",
+                  "rows": 256 * 196, "protos": protos, "features": features}
+        sample = f"{rows} rows of negative_l1 per step, -cdist p=1"
     else:
-        raise SystemExit("reference arm: model or look workloads")
+        from intp_preliminary_b200 import hexgrid
+        from oracle.dense_look_grid import dense_look_grid_np, sampling_tables_np
+
+        tables = sampling_tables_np(hexgrid.offset_row_lattice(14, 14))
+        grid = torch.randn(8, 196, 3, 4, 12, generator=torch.Generator().manual_seed(1234)).numpy()
+        step = lambda: dense_look_grid_np(grid, tables)  # noqa: E731
+        units = (4.0 * (grid.size + 8 * 3 * 196 * 196) + 196 * 196 * 41 * 8 / 256) / 1e9
+        unit, metric, dtype = "GB/s", DenseLookGridWorkload.metric, "f32"
+        config = {"workload": "dense_look_grid: grid (256, 196, 3, 4, 12) fp32 -> bias (256, 3, 196, 196) fp32, "
+                              "14x14 hex lattice tables", "batch": 256, "heads": 3, "queries": 196}
+        sample = "8 of 256 images of dense_look_grid per step through the oracle sampler (numpy float64)"
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
