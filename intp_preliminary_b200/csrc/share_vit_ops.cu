@@ -127,10 +127,7 @@ __device__ __forceinline__ float bf16_at(const __nv_bfloat16* p, int64_t i) { re
 // registers while it walks the CTA's patches.
 // VALUES: also the per-slot Look values (phase 2); without it the kernel writes
 // x and the Look pose only and compiles without the phase-2 registers.
-// STAGED: each warp first copies its kPostTokens / 8 response rows into shared
-// memory with 16-byte cp.async (all in flight at once), then computes from
-// there; without it the scores are read from global memory as they are used.
-template <int D, int LP, bool VALUES, bool STAGED>
+template <int D, int LP, bool VALUES>
 __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_embed_args a) {
   extern __shared__ __align__(16) float smem_post[];
   const int LH = a.look_heads, S = a.slots;
@@ -140,31 +137,12 @@ __global__ void __launch_bounds__(kPostThreads) embed_post_kernel(const svit_emb
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dim = 2 * a.bases;
   const __nv_bfloat16* resp = static_cast<const __nv_bfloat16*>(a.resp);
-  constexpr int kWarps = kPostThreads / 32;
-  const int pitch = (a.bases * D + LP * LH + 7) & ~7;  // staged row length, bf16
-  __nv_bfloat16* staged = nullptr;
-  if constexpr (STAGED) {
-    staged = reinterpret_cast<__nv_bfloat16*>(smem_post + (VALUES ? kPostTokens * LH * LP : 0)) +
-             warp * (kPostTokens / kWarps) * pitch;
-    const uint32_t base = smem_u32(staged);
-    for (int j = 0, t = warp; t < kPostTokens; ++j, t += kWarps) {
-      const int64_t row = row0 + t;
-      if (row >= rows) break;
-      const __nv_bfloat16* src = resp + row * a.resp_stride;
-      for (int c = lane; c < pitch / 8; c += 32)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(base + 2u * (j * pitch + 8 * c)),
-                     "l"(src + 8 * c)
-                     : "memory");
-    }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    __syncwarp();
-  }
 
-  for (int t = warp; t < kPostTokens; t += kWarps) {
+  for (int t = warp; t < kPostTokens; t += kPostThreads / 32) {
     const int64_t row = row0 + t;
     if (row >= rows) break;
     const int64_t b = row / a.patches, n = row - b * a.patches;
-    const __nv_bfloat16* r = STAGED ? staged + (t / kWarps) * pitch : resp + row * a.resp_stride;
+    const __nv_bfloat16* r = resp + row * a.resp_stride;
     float* xrow = a.x + (b * (a.patches + 1) + n + 1) * dim;
     const float* pos = a.pos_embed + (n + 1) * dim;
     for (int p = lane; p < a.bases; p += 32) {
@@ -402,18 +380,11 @@ extern "C" INTP_API intp_status svit_embed_post(const svit_embed_args* a, void* 
   if (!aligned(a->x, 8)) return INTP_ERR_LAYOUT;
   if (a->values && (a->slots % 4 || !aligned(a->slot_fields, 16) || !aligned(a->values, 16))) return INTP_ERR_LAYOUT;
   if (a->look_pose && !aligned(a->look_pose, 16)) return INTP_ERR_LAYOUT;
-  // The pose staging only serves the per-slot products (values): without them
-  // the kernel keeps no pose in shared memory and more CTAs fit on an SM.
-  // 16-byte aligned response rows are staged in shared memory when they fit
-  // (64 KB at the model's 1008 columns).
-  size_t smem = a->values ? static_cast<size_t>(kPostTokens) * a->look_heads * LP * sizeof(float) : 0;
+  // the pose staging only serves the per-slot products (values); without them
+  // the kernel needs no shared memory and more CTAs fit on an SM
+  const size_t smem = a->values ? static_cast<size_t>(kPostTokens) * a->look_heads * LP * sizeof(float) : 0;
   if (smem > 200 * 1024) return INTP_ERR_SHAPE;
-  const size_t pitch = static_cast<size_t>((columns + 7) & ~static_cast<int64_t>(7));
-  const size_t staged_bytes = static_cast<size_t>(kPostTokens) * pitch * sizeof(__nv_bfloat16);
-  const bool staged = aligned(a->resp, 16) && a->resp_stride % 8 == 0 && smem + staged_bytes <= 200 * 1024;
-  if (staged) smem += staged_bytes;
-  auto kernel = a->values ? (staged ? embed_post_kernel<D, LP, true, true> : embed_post_kernel<D, LP, true, false>)
-                          : (staged ? embed_post_kernel<D, LP, false, true> : embed_post_kernel<D, LP, false, false>);
+  auto kernel = a->values ? embed_post_kernel<D, LP, true> : embed_post_kernel<D, LP, false>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return INTP_ERR_LAUNCH;
   const int64_t blocks = (a->batch * a->patches + kPostTokens - 1) / kPostTokens;

@@ -186,35 +186,3 @@ def test_tcgen05_linears_match_cublas_trunk(model, cuda_device):
     assert err <= 5e-2 * plain.abs().max().item(), err
     assert torch.isfinite(fused).all()
 
-
-@pytest.mark.parametrize("per_slot_values", [False, True])
-def test_embed_post_staged_rows_equal_direct_reads(model, cuda_device, per_slot_values):
-    """Response rows with a 16-byte aligned stride are staged in shared memory
-    first; a 1012-element stride is read from global memory as used.  Same
-    arithmetic, so x, the Look pose and the per-slot values are bit-identical
-    (rows 5 x 195 = 975: a ragged last CTA)."""
-    from intp_preliminary_b200.share_vit import BASES, DIRECTIONS, LOOK_HEADS
-    from intp_preliminary_b200.share_vit_ops import embed_post
-    batch, n = 5, model.num_patches
-    g = torch.Generator(cuda_device).manual_seed(21)
-    resp = torch.randn(batch * n, 1008, device=cuda_device, generator=g).to(torch.bfloat16)
-    wide = torch.zeros(batch * n, 1012, dtype=torch.bfloat16, device=cuda_device)
-    wide[:, :1008] = resp
-    _, fields = model._fused_embed_weights(cuda_device)
-    outs = []
-    for r in (resp, wide[:, :1008]):
-        x = torch.empty(batch, n + 1, EMBED_DIM, device=cuda_device)
-        values = (torch.empty(batch, LOOK_HEADS, n, fields.shape[-1], device=cuda_device) if per_slot_values
-                  else None)
-        pose = None if per_slot_values else torch.empty(batch, n, LOOK_HEADS, 2 * DIRECTIONS, device=cuda_device)
-        embed_post(r, batch=batch, patches=n, bases=BASES, directions=DIRECTIONS, look_heads=LOOK_HEADS,
-                   look_poses=2 * DIRECTIONS, token_null=model.patch_embed.null_score.detach().float().contiguous(),
-                   direction_coef=model.direction_coefficients.contiguous(),
-                   output_bias=model.patch_embed.output_bias.detach().float().contiguous(),
-                   cls=model.cls_token.detach().float().reshape(-1).contiguous(),
-                   pos_embed=model.pos_embed.detach().float().reshape(n + 1, EMBED_DIM).contiguous(),
-                   look_null=model.look_bank.null_score.detach().float().contiguous(), slot_fields=fields,
-                   x=x, values=values, look_pose=pose)
-        outs.append((x, values if per_slot_values else pose))
-    assert torch.equal(outs[0][0], outs[1][0])
-    assert torch.equal(outs[0][1], outs[1][1])
