@@ -249,6 +249,24 @@ class LookWorkload:
 
         look_attention_forward(self.q, self.k, self.v, self.pose, self.slots, scale=self.scale, out=self.out)
 
+    @property
+    def backward_flops(self) -> float:  # S = QK^T, dP = dO V^T, dV = P^T dO, dK = dS^T Q, dQ = dS K
+        return 10.0 * self.batch * self.heads * self.seq * self.seq * self.dim
+
+    def backward_prepare(self, seed: int):
+        from intp_preliminary_b200 import look_attention_forward
+
+        self.bwd_out, self.bwd_lse = look_attention_forward(self.q, self.k, self.v, self.pose, self.slots,
+                                                            scale=self.scale, want_lse=True)
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        self.grad_out = torch.randn(self.q.shape, device=self.device, generator=g).to(self.dtype)
+
+    def backward_step(self):
+        from intp_preliminary_b200 import look_attention_backward
+
+        look_attention_backward(self.q, self.k, self.v, self.bwd_out, self.bwd_lse, self.grad_out, self.pose,
+                                self.slots, scale=self.scale)
+
     def e2e_inputs(self):
         return [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.pose)]
 
@@ -315,6 +333,15 @@ class NegativeL1Workload:
         from intp_preliminary_b200 import negative_l1_forward
 
         negative_l1_forward(self.x, self.w, out=self.out)
+
+    def backward_prepare(self, seed: int):
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        self.grad_out = torch.randn(self.out.shape, device=self.device, generator=g)
+
+    def backward_step(self):
+        from intp_preliminary_b200 import negative_l1_backward
+
+        negative_l1_backward(self.x, self.w, self.grad_out)
 
     def e2e_inputs(self):
         return [self.x.cpu().pin_memory(), self.w.cpu().pin_memory()]
@@ -541,6 +568,15 @@ def run_ours(args) -> None:
                                   "sla_tc_kernel" if work.dtype != torch.float32 else "sla_simt_kernel",
                                   "one launch per timed step")
         launches = args.steps
+        # the CUDA-core backward (delta, rows and cols kernels) on the same inputs
+        work.backward_prepare(77 + ctx.rank)
+        bwd_ms = max_over_ranks(statistics.mean(_timed_steps(work.backward_step, args.steps, args.warmup, ctx,
+                                                             flush)), ctx)
+        bwd_tflops = work.backward_flops / (bwd_ms * 1e-3) / 1e12
+        extra["backward"] = {"kernels": "delta_kernel + rows_kernel + cols_kernel (CUDA cores, fp32 accumulation)",
+                             "ms": round(bwd_ms, 4), "tflops": round(bwd_tflops, 3),
+                             "flops": "algorithmic 10*B*H*N^2*D",
+                             "frac_of_bf16_peak": round(bwd_tflops / peaks["bf16_tflops"], 4)}
     elif isinstance(work, DenseLookGridWorkload):
         gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -559,6 +595,12 @@ def run_ours(args) -> None:
                     "note": "FP32-issue bound; fp32_tops is the op rate",
                     "fp32_tops": round(work.flops / (per_launch_ms * 1e-3) / 1e12, 2)}
         launches = args.steps
+        work.backward_prepare(77 + ctx.rank)
+        bwd_ms = max_over_ranks(statistics.mean(_timed_steps(work.backward_step, args.steps, args.warmup, ctx,
+                                                             flush)), ctx)
+        extra["backward"] = {"kernels": "nl1_sign_kernel x 2 (grad_x, grad_w)", "ms": round(bwd_ms, 4),
+                             "fp32_tops": round(2 * work.flops / (bwd_ms * 1e-3) / 1e12, 2),
+                             "ops": "2 x 2*M*P*F (sign and multiply-add, both gradients)"}
 
     # End-to-end through the public API with pinned host buffers.
     host_inputs = work.e2e_inputs()
