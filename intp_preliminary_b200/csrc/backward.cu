@@ -97,13 +97,48 @@ __global__ void __launch_bounds__(256) delta_kernel(const SlaBwdParams bp) {
   if (lane == 0) bp.delta[row] = s;
 }
 
-// Stages `rows` rows of a (B,H,N,D) tensor starting at r0 into smem as fp32 (row stride Dp).
+// Shared-memory row layout: head_dim padded to D4 = a multiple of 4 (zeros
+// past D) so rows are read as float4, and a row stride Dp with Dp / 4 odd, so
+// that the 8 lanes of each quarter-warp reading 16 bytes of 8 different rows
+// hit 8 different 4-bank groups.
+__host__ __device__ constexpr int padded_dim(int D) { return (D + 3) & ~3; }
+__host__ __device__ constexpr int row_stride(int D) {
+  return (padded_dim(D) / 4) % 2 ? padded_dim(D) : padded_dim(D) + 4;
+}
+
+// Stages `rows` rows of a (B,H,N,D) tensor starting at r0 into smem as fp32
+// (row stride Dp; columns D .. D4-1 and rows past N written as 0).
 __device__ __forceinline__ void stage_rows(float* dst, int rows, int Dp, const void* src, const int64_t* st,
                                            int32_t dtype, int64_t b, int64_t h, int64_t r0, int64_t N, int D) {
-  for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
-    const int r = idx / D, d = idx % D;
+  const int D4 = padded_dim(D);
+  for (int idx = threadIdx.x; idx < rows * D4; idx += blockDim.x) {
+    const int r = idx / D4, d = idx % D4;
     const int64_t i = r0 + r;
-    dst[r * Dp + d] = i < N ? load_any(src, b * st[0] + h * st[1] + i * st[2] + d * st[3], dtype) : 0.f;
+    dst[r * Dp + d] = i < N && d < D ? load_any(src, b * st[0] + h * st[1] + i * st[2] + d * st[3], dtype) : 0.f;
+  }
+}
+
+// s[r] += a[r] . x, t[r] += c[r] . y over the padded head dimension for the
+// warp's kRowsPerWarp rows: x, y are this lane's rows (float4 reads), a[r],
+// c[r] the rows shared by the warp (broadcast float4 reads).  The sums run over
+// d in order, one fma per element, as a scalar loop would.
+__device__ __forceinline__ void dot_rows(float (&s)[kRowsPerWarp], float (&t)[kRowsPerWarp], const float* a0,
+                                         const float* c0, int row_stride_a, const float* x, const float* y, int D4) {
+  for (int e = 0; e < D4; e += 4) {
+    const float4 xx = *reinterpret_cast<const float4*>(x + e), yy = *reinterpret_cast<const float4*>(y + e);
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) {
+      const float4 aa = *reinterpret_cast<const float4*>(a0 + r * row_stride_a + e);
+      const float4 cc = *reinterpret_cast<const float4*>(c0 + r * row_stride_a + e);
+      s[r] = fmaf(aa.x, xx.x, s[r]);
+      s[r] = fmaf(aa.y, xx.y, s[r]);
+      s[r] = fmaf(aa.z, xx.z, s[r]);
+      s[r] = fmaf(aa.w, xx.w, s[r]);
+      t[r] = fmaf(cc.x, yy.x, t[r]);
+      t[r] = fmaf(cc.y, yy.y, t[r]);
+      t[r] = fmaf(cc.z, yy.z, t[r]);
+      t[r] = fmaf(cc.w, yy.w, t[r]);
+    }
   }
 }
 
@@ -113,15 +148,16 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y, row0 = static_cast<int64_t>(blockIdx.x) * kRows;
   const int64_t N = p.seq, Np = N - 1;
-  const int D = static_cast<int>(p.head_dim), Dp = D + 1;
+  const int D = static_cast<int>(p.head_dim), D4 = padded_dim(D), Dp = row_stride(D);
   const int P = static_cast<int>(p.poses);
   const int64_t n_kt64 = (N + 63) / 64;
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   float* q_s = smem;                  // kRows x Dp
   float* go_s = q_s + kRows * Dp;     // kRows x Dp
   float* k_s = go_s + kRows * Dp;     // kChunk x Dp
   float* v_s = k_s + kChunk * Dp;     // kChunk x Dp
-  float* dpose_s = v_s + kChunk * Dp; // kRows x P (bias modes 1 and 2)
+  float* ds_tile = v_s + kChunk * Dp; // kRows x kChunk: dS rows of each warp
+  float* dpose_s = ds_tile + kRows * kChunk;  // kRows x P (bias modes 1 and 2)
   stage_rows(q_s, kRows, Dp, p.q, p.q_stride, p.dtype, b, h, row0, N, D);
   stage_rows(go_s, kRows, Dp, bp.grad_out, bp.grad_out_stride, p.dtype, b, h, row0, N, D);
   if (p.bias_mode != 0)
@@ -145,31 +181,26 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
     __syncthreads();
     const int64_t kj = key0 + lane;
     const bool key_ok = kj < N;
+    // S and dP of this lane's key against the warp's rows, together
+    float sv[kRowsPerWarp], dpv[kRowsPerWarp], dsv[kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) sv[r] = dpv[r] = 0.f;
+    dot_rows(sv, dpv, q_s + warp * kRowsPerWarp * Dp, go_s + warp * kRowsPerWarp * Dp, Dp, k_s + lane * Dp,
+             v_s + lane * Dp, D4);
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) {
       const int rr = warp * kRowsPerWarp + r;
       const int64_t i = row0 + rr;
+      dsv[r] = 0.f;
       if (i >= N) continue;  // warp-uniform
-      float s = 0.f, dp = 0.f;
-      for (int d = 0; d < D; ++d) {
-        s = fmaf(q_s[rr * Dp + d], k_s[lane * Dp + d], s);
-        dp = fmaf(go_s[rr * Dp + d], v_s[lane * Dp + d], dp);
-      }
-      s *= p.scale;
+      float s = sv[r] * p.scale;
+      const float dp = dpv[r];
       int slot = -1;
       const bool look = key_ok && i > 0 && kj > 0;
       if (look) s += pair_bias(p, b, h, i, kj, n_kt64, &slot);
       const float prob = key_ok ? expf(s - lse[r]) : 0.f;
       const float ds = prob * (dp - dlt[r]);
-      // dQ += dS K (scale applied at the end)
-      for (int j = 0; j < kChunk; ++j) {
-        const float dsj = __shfl_sync(0xffffffffu, ds, j);
-#pragma unroll
-        for (int t = 0; t < kMaxDim / 32; ++t) {
-          const int d = lane + 32 * t;
-          if (d < D) acc[r][t] = fmaf(dsj, k_s[j * Dp + d], acc[r][t]);
-        }
-      }
+      dsv[r] = ds;
       if (!look) continue;
       const int64_t pq = i - 1, pk = kj - 1;
       if (bp.grad_dense != nullptr) bp.grad_dense[((b * p.heads + h) * Np + pq) * Np + pk] = ds;
@@ -190,6 +221,34 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
         }
       }
     }
+    // dQ += dS K (scale applied at the end): the warp's dS rows go through a
+    // shared tile read four keys at a time (broadcast), each K value is read
+    // once for the warp's rows
+    float* ds_w = ds_tile + warp * kRowsPerWarp * kChunk;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) ds_w[r * kChunk + lane] = dsv[r];
+    __syncwarp();
+    for (int j0 = 0; j0 < kChunk; j0 += 4) {
+      float4 d4[kRowsPerWarp];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) d4[r] = *reinterpret_cast<const float4*>(ds_w + r * kChunk + j0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float kv[kMaxDim / 32];
+#pragma unroll
+        for (int t = 0; t < kMaxDim / 32; ++t) {
+          const int d = lane + 32 * t;
+          kv[t] = d < D ? k_s[(j0 + u) * Dp + d] : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+          const float dsj = u == 0 ? d4[r].x : u == 1 ? d4[r].y : u == 2 ? d4[r].z : d4[r].w;
+#pragma unroll
+          for (int t = 0; t < kMaxDim / 32; ++t) acc[r][t] = fmaf(dsj, kv[t], acc[r][t]);
+        }
+      }
+    }
+    __syncwarp();
   }
   __syncthreads();
 #pragma unroll
@@ -217,15 +276,17 @@ __global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y, key0 = static_cast<int64_t>(blockIdx.x) * kRows;
   const int64_t N = p.seq;
-  const int D = static_cast<int>(p.head_dim), Dp = D + 1;
+  const int D = static_cast<int>(p.head_dim), D4 = padded_dim(D), Dp = row_stride(D);
   const int64_t n_kt64 = (N + 63) / 64;
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   float* k_s = smem;                  // kRows x Dp
   float* v_s = k_s + kRows * Dp;      // kRows x Dp
   float* q_s = v_s + kRows * Dp;      // kChunk x Dp
   float* go_s = q_s + kChunk * Dp;    // kChunk x Dp
-  float* lse_s = go_s + kChunk * Dp;  // kChunk
-  float* dlt_s = lse_s + kChunk;      // kChunk
+  float* p_tile = go_s + kChunk * Dp;       // kRows x kChunk: P rows of each warp
+  float* ds_tile = p_tile + kRows * kChunk;  // kRows x kChunk: dS rows of each warp
+  float* lse_s = ds_tile + kRows * kChunk;   // kChunk
+  float* dlt_s = lse_s + kChunk;             // kChunk
   stage_rows(k_s, kRows, Dp, p.k, p.k_stride, p.dtype, b, h, key0, N, D);
   stage_rows(v_s, kRows, Dp, p.v, p.v_stride, p.dtype, b, h, key0, N, D);
 
@@ -248,34 +309,64 @@ __global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp
     __syncthreads();
     const int64_t i = q0 + lane;  // this lane's query
     const bool q_ok = i < N;
+    // S and dP of this lane's query against the warp's keys, together
+    float sv[kRowsPerWarp], dpv[kRowsPerWarp], pv[kRowsPerWarp], dsv[kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) sv[r] = dpv[r] = 0.f;
+    dot_rows(sv, dpv, k_s + warp * kRowsPerWarp * Dp, v_s + warp * kRowsPerWarp * Dp, Dp, q_s + lane * Dp,
+             go_s + lane * Dp, D4);
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) {
-      const int rr = warp * kRowsPerWarp + r;
-      const int64_t kj = key0 + rr;
+      const int64_t kj = key0 + warp * kRowsPerWarp + r;
+      pv[r] = dsv[r] = 0.f;
       if (kj >= N) continue;  // warp-uniform
-      float s = 0.f, dp = 0.f;
-      for (int d = 0; d < D; ++d) {
-        s = fmaf(q_s[lane * Dp + d], k_s[rr * Dp + d], s);
-        dp = fmaf(go_s[lane * Dp + d], v_s[rr * Dp + d], dp);
-      }
-      s *= p.scale;
+      float s = sv[r] * p.scale;
       int slot;
       if (q_ok && i > 0 && kj > 0) s += pair_bias(p, b, h, i, kj, n_kt64, &slot);
       const float prob = q_ok ? expf(s - lse_s[lane]) : 0.f;
-      const float ds = prob * (dp - dlt_s[lane]);
-      for (int j = 0; j < kChunk; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, prob, j);
-        const float dsj = __shfl_sync(0xffffffffu, ds, j);
+      pv[r] = prob;
+      dsv[r] = prob * (dpv[r] - dlt_s[lane]);
+    }
+    // dV += P^T dO, dK += dS^T Q: the warp's P and dS rows go through shared
+    // tiles read four queries at a time (broadcast), each dO / Q value is read
+    // once for the warp's keys
+    float* p_w = p_tile + warp * kRowsPerWarp * kChunk;
+    float* ds_w = ds_tile + warp * kRowsPerWarp * kChunk;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) {
+      p_w[r * kChunk + lane] = pv[r];
+      ds_w[r * kChunk + lane] = dsv[r];
+    }
+    __syncwarp();
+    for (int j0 = 0; j0 < kChunk; j0 += 4) {
+      float4 p4[kRowsPerWarp], d4[kRowsPerWarp];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        p4[r] = *reinterpret_cast<const float4*>(p_w + r * kChunk + j0);
+        d4[r] = *reinterpret_cast<const float4*>(ds_w + r * kChunk + j0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float gv[kMaxDim / 32], qv[kMaxDim / 32];
 #pragma unroll
         for (int t = 0; t < kMaxDim / 32; ++t) {
           const int d = lane + 32 * t;
-          if (d < D) {
-            dv[r][t] = fmaf(pj, go_s[j * Dp + d], dv[r][t]);
-            dk[r][t] = fmaf(dsj, q_s[j * Dp + d], dk[r][t]);
+          gv[t] = d < D ? go_s[(j0 + u) * Dp + d] : 0.f;
+          qv[t] = d < D ? q_s[(j0 + u) * Dp + d] : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+          const float pj = u == 0 ? p4[r].x : u == 1 ? p4[r].y : u == 2 ? p4[r].z : p4[r].w;
+          const float dsj = u == 0 ? d4[r].x : u == 1 ? d4[r].y : u == 2 ? d4[r].z : d4[r].w;
+#pragma unroll
+          for (int t = 0; t < kMaxDim / 32; ++t) {
+            dv[r][t] = fmaf(pj, gv[t], dv[r][t]);
+            dk[r][t] = fmaf(dsj, qv[t], dk[r][t]);
           }
         }
       }
     }
+    __syncwarp();
   }
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) {
@@ -358,10 +449,12 @@ int32_t launch_sla_backward(const SlaBwdParams& bp, cudaStream_t stream) {
   if (p.heads > 65535 || p.batch > 65535) return 8;
   const int64_t rows = p.batch * p.heads * p.seq;
   delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(bp);
-  const int Dp = static_cast<int>(p.head_dim) + 1;
+  const int Dp = row_stride(static_cast<int>(p.head_dim));
   const int P = p.bias_mode != 0 ? static_cast<int>(p.poses) : 0;
-  const size_t smem_rows = (static_cast<size_t>(2 * kRows + 2 * kChunk) * Dp + kRows * P) * sizeof(float);
-  const size_t smem_cols = (static_cast<size_t>(2 * kRows + 2 * kChunk) * Dp + 2 * kChunk) * sizeof(float);
+  const size_t smem_rows =
+      (static_cast<size_t>(2 * kRows + 2 * kChunk) * Dp + kRows * kChunk + kRows * P) * sizeof(float);
+  const size_t smem_cols =
+      (static_cast<size_t>(2 * kRows + 2 * kChunk) * Dp + 2 * kRows * kChunk + 2 * kChunk) * sizeof(float);
   if (smem_rows > 48 * 1024 &&
       cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rows)) !=
           cudaSuccess)
