@@ -143,7 +143,11 @@ __device__ __forceinline__ void dot_rows(float (&s)[kRowsPerWarp], float (&t)[kR
 }
 
 // dQ, dpose / dslot values, dfields, ddense for 16 query rows of one (b, h).
-__global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp) {
+// TD = head_dim / 32 rounded up (1, 2 or 4): the per-lane accumulator width.
+// Five CTAs per SM (96 registers) keep more warps in flight for the per-pair
+// global loads of the Look lookup.
+template <int TD>
+__global__ void __launch_bounds__(kWarps * 32, 5) rows_kernel(const SlaBwdParams bp) {
   const SlaParams& p = bp.f;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y, row0 = static_cast<int64_t>(blockIdx.x) * kRows;
@@ -163,7 +167,7 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
   if (p.bias_mode != 0)
     for (int idx = threadIdx.x; idx < kRows * P; idx += blockDim.x) dpose_s[idx] = 0.f;
 
-  float lse[kRowsPerWarp], dlt[kRowsPerWarp], acc[kRowsPerWarp][kMaxDim / 32];
+  float lse[kRowsPerWarp], dlt[kRowsPerWarp], acc[kRowsPerWarp][TD];
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) {
     const int64_t i = row0 + warp * kRowsPerWarp + r;
@@ -171,7 +175,7 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
     lse[r] = i < N ? p.lse[bhi] : 0.f;
     dlt[r] = i < N ? bp.delta[bhi] : 0.f;
 #pragma unroll
-    for (int t = 0; t < kMaxDim / 32; ++t) acc[r][t] = 0.f;
+    for (int t = 0; t < TD; ++t) acc[r][t] = 0.f;
   }
 
   for (int64_t key0 = 0; key0 < N; key0 += kChunk) {
@@ -234,9 +238,9 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
       for (int r = 0; r < kRowsPerWarp; ++r) d4[r] = *reinterpret_cast<const float4*>(ds_w + r * kChunk + j0);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        float kv[kMaxDim / 32];
+        float kv[TD];
 #pragma unroll
-        for (int t = 0; t < kMaxDim / 32; ++t) {
+        for (int t = 0; t < TD; ++t) {
           const int d = lane + 32 * t;
           kv[t] = d < D ? k_s[(j0 + u) * Dp + d] : 0.f;
         }
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
         for (int r = 0; r < kRowsPerWarp; ++r) {
           const float dsj = u == 0 ? d4[r].x : u == 1 ? d4[r].y : u == 2 ? d4[r].z : d4[r].w;
 #pragma unroll
-          for (int t = 0; t < kMaxDim / 32; ++t) acc[r][t] = fmaf(dsj, kv[t], acc[r][t]);
+          for (int t = 0; t < TD; ++t) acc[r][t] = fmaf(dsj, kv[t], acc[r][t]);
         }
       }
     }
@@ -256,7 +260,7 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
     const int64_t i = row0 + warp * kRowsPerWarp + r;
     if (i >= N || bp.grad_q == nullptr) continue;
 #pragma unroll
-    for (int t = 0; t < kMaxDim / 32; ++t) {
+    for (int t = 0; t < TD; ++t) {
       const int d = lane + 32 * t;
       if (d < D) bp.grad_q[(((b * p.heads + h) * N) + i) * D + d] = acc[r][t] * p.scale;
     }
@@ -271,7 +275,8 @@ __global__ void __launch_bounds__(kWarps * 32) rows_kernel(const SlaBwdParams bp
 }
 
 // dK, dV for 16 keys of one (b, h): streams query chunks.
-__global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp) {
+template <int TD>
+__global__ void __launch_bounds__(kWarps * 32, 5) cols_kernel(const SlaBwdParams bp) {
   const SlaParams& p = bp.f;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y, key0 = static_cast<int64_t>(blockIdx.x) * kRows;
@@ -290,11 +295,11 @@ __global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp
   stage_rows(k_s, kRows, Dp, p.k, p.k_stride, p.dtype, b, h, key0, N, D);
   stage_rows(v_s, kRows, Dp, p.v, p.v_stride, p.dtype, b, h, key0, N, D);
 
-  float dk[kRowsPerWarp][kMaxDim / 32], dv[kRowsPerWarp][kMaxDim / 32];
+  float dk[kRowsPerWarp][TD], dv[kRowsPerWarp][TD];
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
-    for (int t = 0; t < kMaxDim / 32; ++t) dk[r][t] = dv[r][t] = 0.f;
+    for (int t = 0; t < TD; ++t) dk[r][t] = dv[r][t] = 0.f;
 
   for (int64_t q0 = 0; q0 < N; q0 += kChunk) {
     __syncthreads();
@@ -347,9 +352,9 @@ __global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        float gv[kMaxDim / 32], qv[kMaxDim / 32];
+        float gv[TD], qv[TD];
 #pragma unroll
-        for (int t = 0; t < kMaxDim / 32; ++t) {
+        for (int t = 0; t < TD; ++t) {
           const int d = lane + 32 * t;
           gv[t] = d < D ? go_s[(j0 + u) * Dp + d] : 0.f;
           qv[t] = d < D ? q_s[(j0 + u) * Dp + d] : 0.f;
@@ -359,7 +364,7 @@ __global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp
           const float pj = u == 0 ? p4[r].x : u == 1 ? p4[r].y : u == 2 ? p4[r].z : p4[r].w;
           const float dsj = u == 0 ? d4[r].x : u == 1 ? d4[r].y : u == 2 ? d4[r].z : d4[r].w;
 #pragma unroll
-          for (int t = 0; t < kMaxDim / 32; ++t) {
+          for (int t = 0; t < TD; ++t) {
             dv[r][t] = fmaf(pj, gv[t], dv[r][t]);
             dk[r][t] = fmaf(dsj, qv[t], dk[r][t]);
           }
@@ -373,7 +378,7 @@ __global__ void __launch_bounds__(kWarps * 32) cols_kernel(const SlaBwdParams bp
     const int64_t kj = key0 + warp * kRowsPerWarp + r;
     if (kj >= N) continue;
 #pragma unroll
-    for (int t = 0; t < kMaxDim / 32; ++t) {
+    for (int t = 0; t < TD; ++t) {
       const int d = lane + 32 * t;
       if (d >= D) continue;
       const int64_t o = (((b * p.heads + h) * N) + kj) * D + d;
@@ -455,19 +460,22 @@ int32_t launch_sla_backward(const SlaBwdParams& bp, cudaStream_t stream) {
       (static_cast<size_t>(2 * kRows + 2 * kChunk) * Dp + kRows * kChunk + kRows * P) * sizeof(float);
   const size_t smem_cols =
       (static_cast<size_t>(2 * kRows + 2 * kChunk) * Dp + 2 * kRows * kChunk + 2 * kChunk) * sizeof(float);
+  const int td = p.head_dim <= 32 ? 1 : p.head_dim <= 64 ? 2 : 4;
+  auto rows_k = td == 1 ? rows_kernel<1> : td == 2 ? rows_kernel<2> : rows_kernel<4>;
+  auto cols_k = td == 1 ? cols_kernel<1> : td == 2 ? cols_kernel<2> : cols_kernel<4>;
   if (smem_rows > 48 * 1024 &&
-      cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rows)) !=
+      cudaFuncSetAttribute(rows_k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rows)) !=
           cudaSuccess)
     return 6;
   if (smem_cols > 48 * 1024 &&
-      cudaFuncSetAttribute(cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_cols)) !=
+      cudaFuncSetAttribute(cols_k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_cols)) !=
           cudaSuccess)
     return 6;
   const dim3 grid(static_cast<unsigned>((p.seq + kRows - 1) / kRows), static_cast<unsigned>(p.heads),
                   static_cast<unsigned>(p.batch));
   if (bp.grad_q || bp.grad_pose || bp.grad_fields || bp.grad_dense)
-    rows_kernel<<<grid, kWarps * 32, smem_rows, stream>>>(bp);
-  if (bp.grad_k || bp.grad_v) cols_kernel<<<grid, kWarps * 32, smem_cols, stream>>>(bp);
+    rows_k<<<grid, kWarps * 32, smem_rows, stream>>>(bp);
+  if (bp.grad_k || bp.grad_v) cols_k<<<grid, kWarps * 32, smem_cols, stream>>>(bp);
   return cudaGetLastError() == cudaSuccess ? 0 : 6;
 }
 
