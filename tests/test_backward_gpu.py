@@ -156,3 +156,26 @@ def test_negative_l1_gradients_at_tokenizer_scale(cuda_device):
     (-torch.cdist(xr, wr, p=1)).backward(go.double())
     torch.testing.assert_close(xd.grad.cpu().double(), xr.grad, atol=1e-3, rtol=1e-5)
     torch.testing.assert_close(wd.grad.cpu().double(), wr.grad, atol=1e-3, rtol=1e-5)
+
+
+@pytest.mark.parametrize("head_dim", [20, 40, 96, 128])
+def test_gradients_across_head_dims(cuda_device, head_dim):
+    """The backward kernels are built per head-dim width (up to 32, 64 and 128
+    lanes of accumulators) with the head dimension padded to a multiple of 4 in
+    shared memory: every width and a padded one against float64 autograd through
+    the oracle (general FIELDS form, fp32, the reference's 3e-5)."""
+    g = torch.Generator().manual_seed(head_dim)
+    b, h, patches, poses = 2, 2, 23, 5
+    q, k, v = (torch.randn(b, h, patches + 1, head_dim, generator=g) / 4 for _ in range(3))
+    pose = torch.randn(b, patches, h, poses, generator=g)
+    fields = torch.randn(h, poses, patches, patches, generator=g) / 4
+    grad = torch.randn(b, h, patches + 1, head_dim, generator=g)
+    leaves = [t.to(cuda_device).requires_grad_(True) for t in (q, k, v, pose, fields)]
+    out = structured_look_attention(*leaves, scale=1 / math.sqrt(head_dim))
+    out.backward(grad.to(cuda_device))
+    ref_leaves = [t.double().requires_grad_(True) for t in (q, k, v, pose, fields)]
+    ref = reference_structured_look_attention(*ref_leaves, scale=1 / math.sqrt(head_dim))
+    ref.backward(grad.double())
+    torch.testing.assert_close(out.detach().cpu().double(), ref.detach(), atol=3e-5, rtol=3e-5)
+    for leaf, ref_leaf in zip(leaves, ref_leaves):
+        torch.testing.assert_close(leaf.grad.cpu().double(), ref_leaf.grad, atol=3e-5, rtol=3e-5)
