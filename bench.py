@@ -39,11 +39,15 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-# DRAM bytes (read + write) of one sla_tc_kernel launch at look_cfg4, from the
-# ncu capture summarised in profiles/look_attention_cfg4_tc.md.
+# DRAM bytes (read + write) of one sla_tc_kernel launch at look_cfg4, from one
+# ncu capture of that launch (dram__bytes_read.sum + dram__bytes_write.sum).
 CFG4_TRAFFIC_BYTES = int((202.120704 + 33.865216) * 1e6)
-# Algorithmic FLOPs of one half6d3r image (trunk linears, Look attention QK/PV,
-# tokenizer + Look-bank GEMMs), see DESIGN.md.
+# DRAM bytes (read + write) of one sla_tc_kernel launch on the model forward's
+# inputs (B256 H3 N197, SLOT_FIELDS), from one ncu capture of that launch.
+MODEL_ATTN_TRAFFIC_BYTES = int((70.746368 + 3.088896) * 1e6)
+# Algorithmic FLOPs of one half6d3r image: trunk linears (qkv, proj, fc1, fc2 over
+# 196 tokens, 12 blocks), Look attention QK and PV (4 x 3 heads x 196^2 x 64 per
+# block) and the tokenizer + Look-bank GEMM (195 patches x 1680 x 792).
 MODEL_FLOPS_PER_IMAGE = (196 * 12 * 2 * (192 * 576 + 192 * 192 + 2 * 192 * 768)
                          + 12 * 4 * 3 * 196 * 196 * 64 + 2 * 195 * (1344 + 336) * 792)
 
@@ -545,7 +549,7 @@ def run_ours(args) -> None:
         # (no host gaps), CUDA events around each replay, L2 flushed before it.
         attn_ms = _model_attention_ms(work, args, ctx, flush)
         flops = 4.0 * args.batch * 3 * 196 * 196 * 64
-        roofline = _look_roofline(flops, attn_ms, peaks, None, "sla_tc_kernel",
+        roofline = _look_roofline(flops, attn_ms, peaks, MODEL_ATTN_TRAFFIC_BYTES, "sla_tc_kernel",
                                   "Look attention on the model forward's inputs (B256 H3 N196 D64 bf16, 68 slots, "
                                   "SLOT_FIELDS), the 12 layers' launches replayed as one CUDA graph, per launch")
         # ours per step: hex gather + post-GEMM + the first LayerNorm, then per block
