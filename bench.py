@@ -8,17 +8,26 @@ images/s over all GPUs.  The line also carries the Look-attention kernel timed
 in place inside that forward (``roofline``) and BASELINE config 4 (B64 H6
 N1025 D64 bf16) timed on its own (``look_attention_cfg4``).
 
+``--global-batch G`` fixes the total batch instead (strong scaling: G / N images
+per GPU), the sweep of global batches 256 / 1024 / 4096 over 1 / 2 / 4 / 8 GPUs.
+
 Other workloads: ``look_cfg4`` / ``look_cfg1`` (one Look-attention forward per
-step, TFLOP/s), ``negative_l1`` (M=256*196, P=576, F=1728 fp32) and
-``dense_look_grid`` (dense Look-grid sampling, B256 H3 on the 14x14 lattice,
-fp32 grids -> the (B, H, 196, 196) bias, GB/s; its backward timed alongside).
+step, TFLOP/s), ``negative_l1`` (M=256*196, P=576, F=1728 fp32; ``--features``
+picks 432 or the real 1344 / 336), ``dense_look_grid`` (dense Look-grid
+sampling, B256 H3 on the 14x14 lattice, fp32 grids -> the (B, H, 196, 196)
+bias, GB/s; its backward timed alongside) and ``reference_model`` (the
+reference's own ``DeiTTinyRotHexLook`` half6d3r, unchanged, imported from
+baseline/_ref with this package's operators installed under the reference's
+module names, bf16 autocast, 256 images per GPU).
 
 Contract: ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``;
 for N > 1 launch one process per GPU with torchrun.  Timing: CUDA events on the
 launching stream around every step, L2 flushed (256 MiB write) between steps
 outside the events, barrier + synchronize on both sides of the timed loop, max
 over ranks; rank 0 prints one JSON line.  ``--impl reference`` times the
-reference's CPU algorithm (the oracle port) on bounded samples, rank 0 only.
+reference's CPU implementation on bounded samples, rank 0 only: the
+reference's own model code from baseline/_ref when it is installed
+(``kind: reference``), else the oracle port of its algorithm (``kind: port``).
 """
 
 from __future__ import annotations
@@ -186,20 +195,121 @@ class ModelWorkload:
         return start.elapsed_time(end)
 
     def cpu_reference(self):
+        return _reference_cpu_sample(2)
+
+
+REFERENCE_DIR = ROOT / "baseline" / "_ref"
+HALF6D3R = dict(use_pos_embed=True, directions=6, global_directions=12, angular_bins_per_radius=3,
+                look_compact_variable_rings=True, tokenizer_null_initial_score=0.0)
+
+
+def _reference_model_class(drop_in: bool):
+    """The reference's ``DeiTTinyRotHexLook`` from baseline/_ref, with this
+    package's operators under the reference's module names when ``drop_in``."""
+    if not (REFERENCE_DIR / "model" / "deit_tiny_rot_hex_look.py").exists():
+        return None
+    if str(REFERENCE_DIR) not in sys.path:
+        sys.path.insert(1, str(REFERENCE_DIR))
+    if drop_in:
+        from intp_preliminary_b200.layers.drop_in import install_drop_in
+
+        install_drop_in(polar_render="torch")
+    from model.deit_tiny_rot_hex_look import DeiTTinyRotHexLook
+
+    return DeiTTinyRotHexLook
+
+
+def _reference_half6d3r(drop_in: bool, look_grid_std: float = 0.02):
+    """The reference model with the seeded init of ``ShareViTHalf6d3r.init_weights``."""
+    from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+
+    cls = _reference_model_class(drop_in)
+    if cls is None:
+        return None
+    weights = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=look_grid_std)
+    model = cls(**HALF6D3R).eval()
+    model.load_state_dict(weights.state_dict(), strict=True)
+    return model
+
+
+class ReferenceModelWorkload(ModelWorkload):
+    """The reference's own half6d3r model, unchanged, on this package's operators
+    (bf16 autocast, eager PyTorch around them); logits gathered to rank 0."""
+
+    name = "reference_model"
+    metric = "half6d3r SHARE-ViT DeiT-Tiny inference images/s (reference model code, bf16 autocast)"
+
+    def __init__(self, ctx, per_gpu_batch: int, seed: int):
+        self.ctx = ctx
+        self.device = ctx.device
+        self.batch = per_gpu_batch
+        self.global_batch = per_gpu_batch * ctx.world
+        model = _reference_half6d3r(drop_in=True)
+        if model is None:
+            raise SystemExit("reference_model needs the reference in baseline/_ref "
+                             "(sh baseline/install_reference.sh <checkout>)")
+        self.model = model.to(self.device)
+        g = torch.Generator(device=self.device).manual_seed(seed + ctx.rank)
+        self.images = torch.randn(self.batch, 3, 224, 224, device=self.device, generator=g)
+        self.logits = None
+
+    @property
+    def config(self) -> dict:
+        return {"workload": f"reference_model: the reference's DeiTTinyRotHexLook half6d3r (unchanged model code) "
+                            f"on this package's operators, {self.batch} images of 224x224x3 per GPU, bf16 autocast",
+                "batch_per_gpu": self.batch, "global_batch": self.global_batch, "tokens": 196}
+
+    def forward(self, images):
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return self.model(images)
+
+    def step(self):
+        from intp_preliminary_b200.sharding import gather_to_main
+
+        self.logits = gather_to_main(self.forward(self.images).float(), self.ctx, self.global_batch)
+
+    def e2e_step(self, host_inputs, host_out):
+        from intp_preliminary_b200.sharding import gather_to_main
+
+        images = host_inputs[0].to(self.device, non_blocking=True)
+        logits = gather_to_main(self.forward(images).float(), self.ctx, self.global_batch)
+        if self.ctx.is_main:
+            host_out.copy_(logits, non_blocking=True)
+
+    def e2e_inputs(self):
+        return super().e2e_inputs()[:1]
+
+    def cpu_reference(self):
+        return _reference_cpu_sample(2)
+
+
+def _reference_cpu_sample(count: int, seconds: float = 15.0):
+    """images/s of the reference's own model on the host CPU (all threads),
+    ``count`` images per run; falls back to the oracle port when the reference
+    is not installed.  Returns (value, sample, kind)."""
+    images = torch.randn(count, 3, 224, 224, generator=torch.Generator().manual_seed(1234))
+    model = _reference_half6d3r(drop_in=False)
+    if model is not None:
+        run = lambda: model(images)  # noqa: E731
+        what, kind = f"the reference's own DeiTTinyRotHexLook (baseline/_ref) on CPU, {count} images", "reference"
+    else:
         from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
         from oracle.share_vit_cpu import reference_forward_cpu
 
-        cpu_model = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.02)
-        images = self.images[:2].float().cpu()
-        reference_forward_cpu(cpu_model, images)
-        times, t_end = [], time.perf_counter() + 15.0
+        port = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.02)
+        run = lambda: reference_forward_cpu(port, images)  # noqa: E731
+        what, kind = f"reference CPU algorithm (oracle port: dense fields + explicit attention), {count} images", \
+            "port"
+    with torch.no_grad():
+        run()
+        times, t_end = [], time.perf_counter() + seconds
         while time.perf_counter() < t_end or len(times) < 2:
             t0 = time.perf_counter()
-            reference_forward_cpu(cpu_model, images)
+            run()
             times.append(time.perf_counter() - t0)
             if len(times) >= 20:
                 break
-        return 2 / statistics.median(times), f"reference CPU algorithm (dense fields + explicit oracle), 2 images, median of {len(times)}"
+    return count / statistics.median(times), f"{what}, median of {len(times)}", kind
 
 
 class LookWorkload:
@@ -522,14 +632,22 @@ def run_ours(args) -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ctx.world}; launch N>1 with torchrun")
     device = ctx.device
     peaks = _peaks()
+    scaling = "weak"
+    per_gpu = args.batch
+    if args.global_batch is not None:
+        if args.global_batch % ctx.world:
+            raise SystemExit(f"--global-batch {args.global_batch} does not split over {ctx.world} GPUs")
+        per_gpu, scaling = args.global_batch // ctx.world, "strong"
     if args.workload == "model":
-        work = ModelWorkload(ctx, args.batch, seed=1234)
+        work = ModelWorkload(ctx, per_gpu, seed=1234)
+    elif args.workload == "reference_model":
+        work = ReferenceModelWorkload(ctx, per_gpu, seed=1234)
     elif args.workload.startswith("look"):
         work = LookWorkload(args.workload, device, seed=1234 + ctx.rank, world=ctx.world)
     elif args.workload == "dense_look_grid":
         work = DenseLookGridWorkload(device, seed=1234 + ctx.rank, world=ctx.world)
     else:
-        work = NegativeL1Workload(device, seed=1234 + ctx.rank, world=ctx.world)
+        work = NegativeL1Workload(device, seed=1234 + ctx.rank, world=ctx.world, features=args.features)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
     gpu_index = visible[ctx.local_rank] if ctx.local_rank < len(visible) else str(ctx.local_rank)
@@ -543,15 +661,27 @@ def run_ours(args) -> None:
     per_launch_ms = statistics.mean(times)
 
     extra = {}
-    if isinstance(work, ModelWorkload):
+    if isinstance(work, ReferenceModelWorkload):
+        from intp_preliminary_b200.look_registry import REGISTRY
+
+        hits = REGISTRY.hits
+        work.step()
+        torch.cuda.synchronize(device)
+        roofline = None
+        launches = 12 * args.steps  # this package's: the 12 attention launches (the rest is the reference's PyTorch)
+        extra["look_registry_hits_per_step"] = REGISTRY.hits - hits
+    elif isinstance(work, ModelWorkload):
         # The attention kernel on the model's own inputs: the 12 layers' attention
         # arguments of one forward, replayed as one CUDA graph of 12 launches
         # (no host gaps), CUDA events around each replay, L2 flushed before it.
         attn_ms = _model_attention_ms(work, args, ctx, flush)
-        flops = 4.0 * args.batch * 3 * 196 * 196 * 64
-        roofline = _look_roofline(flops, attn_ms, peaks, MODEL_ATTN_TRAFFIC_BYTES, "sla_tc_kernel",
-                                  "Look attention on the model forward's inputs (B256 H3 N196 D64 bf16, 68 slots, "
-                                  "SLOT_FIELDS), the 12 layers' launches replayed as one CUDA graph, per launch")
+        flops = 4.0 * work.batch * 3 * 196 * 196 * 64
+        roofline = _look_roofline(flops, attn_ms, peaks,
+                                  MODEL_ATTN_TRAFFIC_BYTES if work.batch == 256 else None,
+                                  "sla_tc_kernel",
+                                  f"Look attention on the model forward's inputs (B{work.batch} H3 N196 D64 bf16, "
+                                  "68 slots, SLOT_FIELDS), the 12 layers' launches replayed as one CUDA graph, "
+                                  "per launch")
         # ours per step: hex gather + post-GEMM + the first LayerNorm, then per block
         # qkv, Look attention, proj + residual + LN, fc1 + GELU, fc2 + residual + LN
         # (the tokenizer GEMM and the classifier head are cuBLAS)
@@ -609,7 +739,11 @@ def run_ours(args) -> None:
     # End-to-end through the public API with pinned host buffers.
     host_inputs = work.e2e_inputs()
     host_out = work.e2e_output()
-    if isinstance(work, ModelWorkload):
+    if isinstance(work, ReferenceModelWorkload):
+        e2e_times = _timed_steps(lambda: work.e2e_step(host_inputs, host_out), args.steps, args.warmup, ctx, flush)
+        e2e_total = max_over_ranks(sum(e2e_times), ctx)
+        h2d = host_inputs[0].numel() * host_inputs[0].element_size()
+    elif isinstance(work, ModelWorkload):
         # Batches stream from host memory (each step copies its own 154 MB
         # batch, larger than L2); copies overlap the previous step's forward.
         work.e2e_run(host_inputs, host_out, args.warmup)
@@ -625,18 +759,19 @@ def run_ours(args) -> None:
 
     cpu = None
     if ctx.is_main and not args.no_cpu_baseline:
-        cpu_value, sample = work.cpu_reference()
-        cpu = {"value": round(cpu_value, 6), "unit": work.unit, "cores": torch.get_num_threads(), "kind": "port",
-               "sample": sample}
+        result = work.cpu_reference()
+        cpu_value, sample = result[:2]
+        cpu = {"value": round(cpu_value, 6), "unit": work.unit, "cores": torch.get_num_threads(),
+               "kind": result[2] if len(result) > 2 else "port", "sample": sample}
     if ctx.is_main:
         line = {
             "metric": work.metric, "value": round(value, 3), "unit": work.unit, "n_gpus": ctx.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": {torch.bfloat16: "bf16", torch.float32: "f32"}[work.dtype],
             "data": "synthetic (seeded; BASELINE shapes and distributions, random-init weights)",
             "config": {**work.config,
-                       "parallelism": f"batch-sharded replicas x{ctx.world} (weak), logits gathered to rank 0"
+                       "parallelism": f"batch-sharded replicas x{ctx.world} ({scaling}), logits gathered to rank 0"
                        if isinstance(work, ModelWorkload) else f"independent replicas x{ctx.world} (weak)",
                        "l2": "flushed between steps (256 MiB write outside the timed events)"},
             "roofline": roofline,
@@ -656,18 +791,29 @@ def run_reference(args) -> None:
     if int(os.environ.get("RANK", "0")) != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    if args.workload == "model":
-        from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
-        from oracle.share_vit_cpu import reference_forward_cpu
-
-        model = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.02)
+    kind = "port"
+    if args.workload in ("model", "reference_model"):
         images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(1234))
-        step = lambda: reference_forward_cpu(model, images)  # noqa: E731
+        model = _reference_half6d3r(drop_in=False)
+        if model is not None:
+            def step():
+                with torch.no_grad():
+                    model(images)
+
+            kind = "reference"
+            sample = "2 images per step through the reference's own DeiTTinyRotHexLook (baseline/_ref) on CPU"
+        else:
+            from intp_preliminary_b200.share_vit import ShareViTHalf6d3r
+            from oracle.share_vit_cpu import reference_forward_cpu
+
+            port = ShareViTHalf6d3r(precision="fp32").init_weights(seed=0, look_grid_std=0.02)
+            step = lambda: reference_forward_cpu(port, images)  # noqa: E731
+            sample = "2 images per step through the reference CPU algorithm (oracle port: dense fields + explicit attention)"
         units, unit = 2.0, "images/s"
-        metric = ModelWorkload.metric
-        config = {"workload": f"model: half6d3r SHARE-ViT DeiT-Tiny forward, {args.batch} images per GPU",
-                  "batch_per_gpu": args.batch}
-        sample = "2 images per step through the reference CPU algorithm (dense fields + explicit oracle)"
+        metric = ReferenceModelWorkload.metric if args.workload == "reference_model" else ModelWorkload.metric
+        per_gpu = args.global_batch // args.gpus if args.global_batch else args.batch
+        config = {"workload": f"{args.workload}: half6d3r SHARE-ViT DeiT-Tiny forward, {per_gpu} images per GPU",
+                  "batch_per_gpu": per_gpu}
         dtype = "f32"
     elif args.workload.startswith("look"):
         work = _CpuLook(args.workload)
@@ -707,9 +853,9 @@ def run_reference(args) -> None:
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-        "config": config,
-        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+        "higher_is_better": True, "scaling": "strong" if args.global_batch else "weak", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic", "config": config,
+        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": torch.get_num_threads(), "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -752,9 +898,12 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["model", "look_cfg4", "look_cfg1", "negative_l1", "dense_look_grid"],
-                        default="model")
-    parser.add_argument("--batch", type=int, default=256, help="images per GPU (model workload)")
+    parser.add_argument("--workload", choices=["model", "reference_model", "look_cfg4", "look_cfg1", "negative_l1",
+                                               "dense_look_grid"], default="model")
+    parser.add_argument("--batch", type=int, default=256, help="images per GPU (model workloads, weak scaling)")
+    parser.add_argument("--global-batch", type=int, default=None,
+                        help="total images over all GPUs (model workloads, strong scaling)")
+    parser.add_argument("--features", type=int, default=1728, help="negative_l1 feature size F")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     if args.warmup < 3:

@@ -214,8 +214,10 @@ INTP_API intp_status dlg_forward(const dlg_args* args, void* stream);
 INTP_API intp_status dlg_backward(const dlg_args* args, const void* grad_out, const dlg_grad_strides* grad_strides,
                                   void* grad_grid, void* stream);
 
-/* Copies the device status word written by bounded waits to the host
- * (synchronous on `stream`) and clears it.  *code = 0 when no wait failed.  */
+/* Copies the device status word to the host (synchronous on `stream`) and
+ * clears it.  *code = 0 and INTP_OK when nothing was recorded; code 0x201 (a
+ * slot byte out of range in sla_forward_noalloc) returns INTP_ERR_ARGUMENT;
+ * every other code is a bounded wait that gave up (INTP_ERR_TIMEOUT).        */
 INTP_API intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream);
 
 /* Longest sequence (tokens, CLS included) sla_forward_noalloc accepts. */
@@ -230,19 +232,28 @@ INTP_API intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* s
  *
  * Same arguments as sla_forward in SLOTS mode on the tensor-core path (bf16 or
  * f16, head_dim 64), except that `slots` is the plain (Np x Np) uint8 slot
- * table in device memory (SLA_SLOT_NONE = no bias; other values >= n_slots
- * are also taken as no bias); args->slots_packed and args->slot_tile_flags
- * are ignored.  The table is packed on the GPU into a library-owned
- * file-scope __device__ scratch array of about 1.2 MB, which every GPU that
- * loads the library holds until the process exits.  args->status may point
- * at a caller-owned int32 that receives bounded-wait failures; when it is
- * NULL they are recorded in the scratch instead.
+ * table in device memory (SLA_SLOT_NONE = no bias); args->slots_packed and
+ * args->slot_tile_flags are ignored.  The table is packed on the GPU into a
+ * library-owned file-scope __device__ scratch array of about 1.2 MB, which
+ * every GPU that loads the library holds until the process exits.
+ *
+ * Errors: the host-side checks of sla_forward (null q / k / v / out / pose,
+ * dtype codes, kernel selector, unit head_dim stride) run first and a
+ * rejected call launches nothing.  Errors found on the GPU go to the int32
+ * status word: args->status, a caller-owned device int32 (read it with
+ * sla_read_status), receives bounded-wait failures (INTP_ERR_TIMEOUT) and a
+ * slot byte >= n_slots other than SLA_SLOT_NONE (INTP_ERR_ARGUMENT; that
+ * pair then gets no bias, where sla_pack_slot_table would have refused the
+ * table).  When args->status is NULL these are recorded in the scratch, which
+ * no call exposes: callers that need to learn of them pass a status word.
  *
  * Limits and behaviour:
  *   - seq > SLA_NOALLOC_MAX_SEQ, or a request the tensor-core path cannot
  *     take, returns INTP_ERR_UNSUPPORTED without launching anything.
  *   - The first call on each device resolves the scratch address with that
- *     device current; make that first call before any stream capture.
+ *     device current and caches it for the process; make that first call
+ *     before any stream capture, and do not use this entry point across a
+ *     cudaDeviceReset (the cached address belongs to the old context).
  *   - Every call shares the scratch and leaves its contents behind; calls
  *     whose work overlaps on the GPU (several streams or threads) race.
  *   - Calls no cudaMalloc / cudaFree and no allocating library routine.      */

@@ -275,7 +275,9 @@ intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* stream) {
   *code = host;
   if (host != 0) {
     if (cudaMemsetAsync(status_dev, 0, sizeof(int32_t), s) != cudaSuccess) return INTP_ERR_LAUNCH;
-    return INTP_ERR_TIMEOUT;
+    // 0x201: sla_forward_noalloc met a slot byte >= n_slots (not SLA_SLOT_NONE);
+    // every other code is a bounded wait that gave up.
+    return host == 0x201 ? INTP_ERR_ARGUMENT : INTP_ERR_TIMEOUT;
   }
   return INTP_OK;
 }

@@ -33,6 +33,8 @@ constexpr int64_t kFlagsOffset = kPackedBytes;
 constexpr int64_t kStatusOffset = kFlagsOffset + 256;  // flags need kMaxQTiles * kMaxKTiles = 153 bytes
 constexpr int64_t kScratchBytes = kStatusOffset + 256;
 static_assert(kMaxQTiles * kMaxKTiles <= 256, "flag area too small");
+// Status-word code of a slot byte >= n_slots that is not SLA_SLOT_NONE.
+constexpr int32_t kDevBadSlot = 0x201;
 
 // The library-owned scratch.  In host code `g_scratch` is only a host-side
 // stand-in for the symbol: its device address comes from cudaGetSymbolAddress.
@@ -73,7 +75,8 @@ const DeviceScratch* scratch_for_current_device() {
 // writes one "needs lookup" flag per tile.  One
 // thread block per tile; every byte of the used tiles and flags is written.
 __global__ void pack_slots_kernel(const uint8_t* __restrict__ slots, int64_t patch_count, int32_t n_slots,
-                                  int64_t n_kt, uint8_t* __restrict__ packed, uint8_t* __restrict__ flags) {
+                                  int64_t n_kt, uint8_t* __restrict__ packed, uint8_t* __restrict__ flags,
+                                  int32_t* status) {
   const int64_t tile = blockIdx.x;
   const int64_t qt = tile / n_kt, kt = tile % n_kt;
   uint8_t* dst = packed + tile * intp::kSlotTileBytes;
@@ -94,6 +97,10 @@ __global__ void pack_slots_kernel(const uint8_t* __restrict__ slots, int64_t pat
       if (s != SLA_SLOT_NONE && s < n_slots) {
         v = s;
         mine |= 1u << (r / 32);
+      } else if (s != SLA_SLOT_NONE) {
+        // sla_pack_slot_table rejects this byte; here the pair gets no bias
+        // and the status word says so (sla_read_status: INTP_ERR_ARGUMENT).
+        atomicCAS(status, 0, kDevBadSlot);
       }
     }
     dst[e] = v;
@@ -106,13 +113,21 @@ __global__ void pack_slots_kernel(const uint8_t* __restrict__ slots, int64_t pat
 }  // namespace
 
 extern "C" INTP_API intp_status sla_forward_noalloc(const sla_forward_args* a, const uint8_t* slots, void* stream) {
+  // The checks sla_forward makes, in its order, before anything is looked up
+  // or launched: a rejected call touches no device memory.
   if (!a || !slots) return INTP_ERR_ARGUMENT;
+  if (a->batch < 0 || a->heads < 0 || a->seq < 2 || a->head_dim < 1) return INTP_ERR_SHAPE;
+  if (a->dtype != INTP_F32 && a->dtype != INTP_F16 && a->dtype != INTP_BF16) return INTP_ERR_DTYPE;
+  if (a->kernel < SLA_KERNEL_AUTO || a->kernel > SLA_KERNEL_TCGEN05) return INTP_ERR_ARGUMENT;
   if (a->bias_mode != SLA_BIAS_SLOTS || a->dense != nullptr || a->kernel == SLA_KERNEL_SIMT)
     return INTP_ERR_UNSUPPORTED;
-  if (a->seq < 2 || a->batch < 0 || a->heads < 0) return INTP_ERR_SHAPE;
   if (a->seq > kMaxSeq) return INTP_ERR_UNSUPPORTED;  // beyond the scratch capacity
-  if (a->poses < 1 || a->poses > 253 || !a->pose) return INTP_ERR_ARGUMENT;
   if (a->batch == 0 || a->heads == 0) return INTP_OK;
+  if (!a->q || !a->k || !a->v || !a->out || !a->pose) return INTP_ERR_ARGUMENT;
+  if (a->poses < 1 || a->poses > 253) return INTP_ERR_ARGUMENT;
+  if (a->pose_dtype != INTP_F32 && a->pose_dtype != INTP_F16 && a->pose_dtype != INTP_BF16) return INTP_ERR_DTYPE;
+  if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 || a->out_stride[3] != 1)
+    return INTP_ERR_LAYOUT;
   const DeviceScratch* d = scratch_for_current_device();
   if (!d) return INTP_ERR_ARCH;
 
@@ -154,7 +169,7 @@ extern "C" INTP_API intp_status sla_forward_noalloc(const sla_forward_args* a, c
   // whose work overlaps on the GPU (other streams, other threads) race on it.
   if (cudaMemsetAsync(d->base + kStatusOffset, 0, sizeof(int32_t), s) != cudaSuccess) return INTP_ERR_LAUNCH;
   pack_slots_kernel<<<static_cast<unsigned>(n_qt * n_kt), 256, 0, s>>>(
-      slots, patch_count, static_cast<int32_t>(a->poses), n_kt, d->base, d->base + kFlagsOffset);
+      slots, patch_count, static_cast<int32_t>(a->poses), n_kt, d->base, d->base + kFlagsOffset, p.status);
   if (cudaGetLastError() != cudaSuccess) return INTP_ERR_LAUNCH;
   return intp::launch_sla_tc(p, s, d->sms);
 }

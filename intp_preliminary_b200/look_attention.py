@@ -393,7 +393,14 @@ class _StructuredLookAttention(torch.autograd.Function):
 
 
 def structured_look_attention(q, k, v, pose, fields, *, scale, dense_bias=None):
-    """Memory-bounded Look attention forward (layers/triton_structured_look_attention.py:412-424)."""
+    """Memory-bounded Look attention forward (layers/triton_structured_look_attention.py:412-424).
+
+    A dense ``fields`` tensor that is a layer slice of a hooked Look layer's
+    ``transformed_look_grids()`` result runs in its compact slot form
+    (``look_registry``); any other dense tensor runs the general form."""
+    from .look_registry import compact_fields
+
+    fields = compact_fields(fields)
     values = fields.values if isinstance(fields, LookSlotFields) else fields
     if not torch.is_grad_enabled() or not any(
         t.requires_grad for t in (q, k, v, pose, values, dense_bias) if isinstance(t, torch.Tensor)
