@@ -678,7 +678,7 @@ def run_ours(args) -> None:
         flops = 4.0 * work.batch * 3 * 196 * 196 * 64
         roofline = _look_roofline(flops, attn_ms, peaks,
                                   MODEL_ATTN_TRAFFIC_BYTES if work.batch == 256 else None,
-                                  "sla_tc_kernel",
+                                  "sla_short_kernel",
                                   f"Look attention on the model forward's inputs (B{work.batch} H3 N196 D64 bf16, "
                                   "68 slots, SLOT_FIELDS), the 12 layers' launches replayed as one CUDA graph, "
                                   "per launch")

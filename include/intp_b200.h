@@ -259,6 +259,16 @@ INTP_API intp_status sla_read_status(int32_t* status_dev, int32_t* code, void* s
  *   - Calls no cudaMalloc / cudaFree and no allocating library routine.      */
 INTP_API intp_status sla_forward_noalloc(const sla_forward_args* args, const uint8_t* slots, void* stream);
 
+/* Wall-clock budget (nanoseconds, 1 .. 1e9; default 1e9 = one second) of the
+ * pipeline waits of the tensor-core Look-attention kernels, for the launches
+ * that follow (process-wide).  A wait that runs out raises the kernel's abort
+ * flag: every role stops, in-flight copies and MMAs are drained under the full
+ * one-second budget, tensor memory is freed and the status word receives the
+ * role's code (sla_read_status then returns INTP_ERR_TIMEOUT); the output of
+ * that launch is unspecified.  A short budget makes that path testable
+ * without a hung wait.                                                      */
+INTP_API intp_status intp_set_wait_budget_ns(uint64_t budget_ns);
+
 /* Library / device facts: compute capability of the current device and the
  * library's ABI version.                                                    */
 INTP_API intp_status intp_device_info(int32_t* sm_major, int32_t* sm_minor, int32_t* sm_count);

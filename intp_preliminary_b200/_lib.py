@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "sla_forward_noalloc",
     "dlg_forward",
     "dlg_backward",
+    "intp_set_wait_budget_ns",
     "intp_device_info",
     "intp_abi_version",
     "intp_status_string",
@@ -188,6 +189,8 @@ def load() -> ctypes.CDLL:
         lib.dlg_backward.restype = _i32
         lib.sla_read_status.argtypes = [_vp, ctypes.POINTER(_i32), _vp]
         lib.sla_read_status.restype = _i32
+        lib.intp_set_wait_budget_ns.argtypes = [ctypes.c_uint64]
+        lib.intp_set_wait_budget_ns.restype = _i32
         lib.intp_device_info.argtypes = [ctypes.POINTER(_i32)] * 3
         lib.intp_device_info.restype = _i32
         lib.svit_gather_patches.argtypes = [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp]

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include "../../include/intp_b200.h"
 #include "sla_internal.h"
@@ -42,7 +43,13 @@ bool device_facts(DeviceFacts* f) {
 
 bool valid_dtype(int32_t d) { return d == INTP_F32 || d == INTP_F16 || d == INTP_BF16; }
 
+std::atomic<uint64_t> g_wait_budget_ns{1000000000ull};
+
 }  // namespace
+
+namespace intp {
+uint64_t tc_wait_budget_ns() { return g_wait_budget_ns.load(std::memory_order_relaxed); }
+}  // namespace intp
 
 extern "C" {
 
@@ -61,6 +68,12 @@ const char* intp_status_string(intp_status s) {
     case INTP_ERR_UNSUPPORTED: return "request outside kernel coverage";
     default: return "unknown status";
   }
+}
+
+intp_status intp_set_wait_budget_ns(uint64_t budget_ns) {
+  if (budget_ns == 0 || budget_ns > 1000000000ull) return INTP_ERR_ARGUMENT;
+  g_wait_budget_ns.store(budget_ns, std::memory_order_relaxed);
+  return INTP_OK;
 }
 
 intp_status intp_device_info(int32_t* sm_major, int32_t* sm_minor, int32_t* sm_count) {

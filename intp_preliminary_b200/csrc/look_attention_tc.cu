@@ -39,6 +39,8 @@
 #include "sla_internal.h"
 #include "sm100_ptx.cuh"
 #include "tma_host.h"
+#include "sla_tc_common.cuh"
+#include "sla_look_table.cuh"
 
 namespace intp {
 namespace {
@@ -54,12 +56,11 @@ constexpr uint32_t kKVBytes = BN * HD * 2;     // 8 KB each of K and V (and the 
 constexpr uint32_t kSlotBytes = kSlotTileBytes;  // 8 KB
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128;
-constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLog2e = kLog2eF;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 2^8
-constexpr int kMaxSlots = 93;
-constexpr int kMaxPoses = 16;      // SLOT_FIELDS: Look poses per head
-constexpr int kModelPoses = 12;    // the half6d3r Look bank: 2 supports x 6 directions
+constexpr int kMaxSlots = kMaxLookSlots;
+constexpr int kMaxPoses = kMaxLookPoses;
 template <int KS>
 struct alignas(8) Barriers {
   uint64_t q_full, q_empty;
@@ -88,25 +89,6 @@ struct SmemLayout {
   static constexpr uint32_t slots = ones + kKVBytes;
   static constexpr uint32_t table = slots + KS * kSlotBytes;
 };
-
-__device__ __forceinline__ float load_any(const void* p, int64_t idx, int32_t dtype) {
-  switch (dtype) {
-    case 1: return __half2float(static_cast<const __half*>(p)[idx]);
-    case 2: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
-    default: return static_cast<const float*>(p)[idx];
-  }
-}
-
-// Position (1..3) of the row / head / batch coordinate in a tensor map whose
-// outer dimensions are sorted by increasing stride (dimension 0 is head_dim).
-struct MapOrder {
-  int8_t row, head, batch;
-};
-
-// TMA coordinates {0, c1, c2, c3} with row / head / batch placed per `o`.
-__device__ __forceinline__ int32_t map_coord(const MapOrder& o, int pos, int32_t row, int32_t head, int32_t batch) {
-  return o.row == pos ? row : (o.head == pos ? head : batch);
-}
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
@@ -159,206 +141,8 @@ struct TcArgs {
   int32_t sf_vec4;        // SLOT_FIELDS: slot_fields rows are 16-byte aligned fp32, unit slot stride;
                           // the head's rows are then staged in smem after the table
   uint32_t sf_offset;     // SLOT_FIELDS with sf_vec4: floats from the table start to the staged rows
+  uint64_t wait_ns;       // budget of the pipeline waits (drains keep the default)
 };
-
-// Per-query Look values of query token i into column `row` of the [slot][row]
-// table (bank = row % 32: conflict free), pre-scaled to the log2 domain, plus
-// the "no bias" (0) and "past the end" (-inf) entries.  Only this thread reads
-// its column.
-__device__ __forceinline__ void stage_table(float* table_s, const TcArgs& a, int64_t b, int64_t h, int64_t i,
-                                            int row) {
-  const SlaParams& p = a.p;
-  const int32_t ns = a.n_slots;
-  const bool valid = i >= 1 && i < p.seq;
-  const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
-  if (a.pose_vec4) {
-    // The whole row's 16-byte loads in flight at once: one memory round trip
-    // (an L2 hit when the previous item prefetched it).
-    constexpr int kMaxVec = kMaxSlots / 4;
-    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
-    float4 v4[kMaxVec];
-#pragma unroll
-    for (int u = 0; u < kMaxVec; ++u)
-      v4[u] = (valid && u < ns / 4) ? __ldg(src + u) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int u = 0; u < kMaxVec; ++u) {
-      if (u < ns / 4) {
-        float* dst = table_s + 4 * u * BM + row;
-        dst[0] = v4[u].x * kLog2e;
-        dst[BM] = v4[u].y * kLog2e;
-        dst[2 * BM] = v4[u].z * kLog2e;
-        dst[3 * BM] = v4[u].w * kLog2e;
-      }
-    }
-  } else {
-    for (int s = 0; s < ns; ++s)
-      table_s[s * BM + row] = valid ? load_any(p.pose, base + s * p.pose_stride[3], p.pose_dtype) * kLog2e : 0.f;
-  }
-  table_s[ns * BM + row] = 0.f;               // "no bias"
-  table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
-}
-
-// SLOT_FIELDS with sf_vec4: the 128 softmax threads copy head h's slot values
-// (P rows of S fp32) into shared memory after the table; each warp then
-// arrives on sf_ready.  The copy of item k + 1 cannot overwrite rows another
-// warp still reads for item k: a warp reaches item k + 1 only after every
-// warp published all P tiles of item k, i.e. finished its table of item k.
-__device__ __forceinline__ void stage_slot_fields(float* table_s, const TcArgs& a, int64_t h, int tid) {
-  const SlaParams& p = a.p;
-  const int groups = a.n_slots / 4, total = a.n_poses * groups;
-  const float* src = static_cast<const float*>(p.fields) + h * p.fields_stride[0];
-  float4* dst = reinterpret_cast<float4*>(table_s + a.sf_offset);
-  for (int idx = tid; idx < total; idx += BM) {
-    const int pp = idx / groups, s4 = idx - pp * groups;
-    dst[idx] = __ldg(reinterpret_cast<const float4*>(src + pp * p.fields_stride[1]) + s4);
-  }
-}
-
-// SLOT_FIELDS: query token i's Look pose row (raw values; rows past the
-// sequence and the CLS token read as 0).  Issued before the slot values are
-// staged so that the two memory round trips overlap.
-__device__ __forceinline__ void load_pose_row(float (&w)[kMaxPoses], const TcArgs& a, int64_t b, int64_t h,
-                                              int64_t i) {
-  const SlaParams& p = a.p;
-  const int32_t np = a.n_poses;
-  const bool valid = i >= 1 && i < p.seq;
-  const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
-  if (a.pose_vec4) {
-    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.pose) + (valid ? base : 0));
-#pragma unroll
-    for (int c = 0; c < kMaxPoses / 4; ++c) {
-      const float4 v = (valid && 4 * c < np) ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      w[4 * c] = v.x;
-      w[4 * c + 1] = v.y;
-      w[4 * c + 2] = v.z;
-      w[4 * c + 3] = v.w;
-    }
-  } else if (p.pose_dtype == 0) {
-    const float* src = static_cast<const float*>(p.pose);
-#pragma unroll
-    for (int pp = 0; pp < kMaxPoses; ++pp)
-      w[pp] = (valid && pp < np) ? __ldg(src + base + pp * p.pose_stride[3]) : 0.f;
-  } else {
-#pragma unroll
-    for (int pp = 0; pp < kMaxPoses; ++pp)
-      w[pp] = (valid && pp < np) ? load_any(p.pose, base + pp * p.pose_stride[3], p.pose_dtype) : 0.f;
-  }
-}
-
-// Table columns of one warp in SLOT_FIELDS mode.  Lane (gp = lane / 8,
-// rb = lane % 8) takes rows rb + 8 ((gp + m) % 4), m = 0..3 (their poses by
-// shuffle from the owning lanes) and the 4-slot groups gp, gp + 4, ...: each
-// 16-byte slot-value load feeds four rows (16 independent FMA chains), and for a
-// fixed m the 32 lanes store to 32 different rows (banks).  P, the number of
-// poses, is a compile-time constant (no per-pose tests).
-template <int P>
-__device__ __forceinline__ void build_rows_sf(float* col0, const float4* sf, int groups, int lane, int gp, int rb,
-                                              const float (&w)[kMaxPoses]) {
-  int rows[4];
-  float wr[4][P];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    rows[m] = rb + 8 * ((gp + m) & 3);
-#pragma unroll
-    for (int pp = 0; pp < P; ++pp) wr[m][pp] = __shfl_sync(0xffffffffu, w[pp], rows[m]);
-  }
-  (void)lane;
-  for (int g = gp; g < groups; g += 4) {
-    float acc[4][4];
-#pragma unroll
-    for (int m = 0; m < 4; ++m)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[m][k] = 0.f;
-#pragma unroll
-    for (int pp = 0; pp < P; ++pp) {
-      const float4 f = sf[pp * groups + g];
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        acc[m][0] = fmaf(wr[m][pp], f.x, acc[m][0]);
-        acc[m][1] = fmaf(wr[m][pp], f.y, acc[m][1]);
-        acc[m][2] = fmaf(wr[m][pp], f.z, acc[m][2]);
-        acc[m][3] = fmaf(wr[m][pp], f.w, acc[m][3]);
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      float* dst = col0 + 4 * g * BM + rows[m];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) dst[k * BM] = acc[m][k];
-    }
-  }
-}
-
-// SLOT_FIELDS: the per-query table built from the query's Look pose and the
-// head's slot fields, table[s][row] = log2(e) sum_p pose[b,i-1,h,p]
-// slot_fields[h,p,s] (model/deit_tiny_rot_hex_look.py:397-451 feeds exactly
-// this product to the attention as pose x fields).  With sf_vec4 the slot
-// values come from shared memory (stage_slot_fields) and each lane computes
-// four rows of its warp (see below); otherwise each thread computes its own
-// row from global memory.
-__device__ __forceinline__ void build_table_sf(float* table_s, const TcArgs& a, int64_t h, int row,
-                                               float (&w)[kMaxPoses]) {
-  const SlaParams& p = a.p;
-  const int32_t ns = a.n_slots, np = a.n_poses;
-#pragma unroll
-  for (int pp = 0; pp < kMaxPoses; ++pp) w[pp] *= kLog2e;
-  if (a.sf_vec4) {
-    // A warp builds its own 32 table columns.  Lane (gp = lane / 8, rb = lane % 8)
-    // takes rows rb + 8 ((gp + m) % 4), m = 0..3 (their poses by shuffle from the
-    // owning lanes), and the 4-slot groups gp, gp + 4, ...: each 16-byte slot-value
-    // load feeds four rows, and for a fixed m the 32 lanes store to 32 different
-    // rows (banks).
-    const float4* sf = reinterpret_cast<const float4*>(table_s + a.sf_offset);
-    const int groups = ns / 4;
-    const int lane = row & 31, gp = lane >> 3, rb = lane & 7;
-    float* col0 = table_s + (row - lane);  // column of the warp's first row
-    if (np == kModelPoses) {
-      build_rows_sf<kModelPoses>(col0, sf, groups, lane, gp, rb, w);
-    } else {
-      // other pose counts: each thread its own row, one 4-slot group at a time
-      for (int g = 0; g < groups; ++g) {
-        float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int pp = 0; pp < kMaxPoses; ++pp) {
-          if (pp < np) {
-            const float4 f = sf[pp * groups + g];
-            lo = fma2(make_float2(w[pp], w[pp]), make_float2(f.x, f.y), lo);
-            hi = fma2(make_float2(w[pp], w[pp]), make_float2(f.z, f.w), hi);
-          }
-        }
-        float* dst = col0 + 4 * g * BM + lane;
-        dst[0] = lo.x;
-        dst[BM] = lo.y;
-        dst[2 * BM] = hi.x;
-        dst[3 * BM] = hi.y;
-      }
-    }
-    __syncwarp();
-  } else {
-    for (int s = 0; s < ns; ++s) {
-      float acc = 0.f;
-#pragma unroll
-      for (int pp = 0; pp < kMaxPoses; ++pp)
-        if (pp < np)
-          acc = fmaf(w[pp],
-                     load_any(p.fields, h * p.fields_stride[0] + pp * p.fields_stride[1] + s * p.fields_stride[2],
-                              p.fields_dtype),
-                     acc);
-      table_s[s * BM + row] = acc;
-    }
-  }
-  table_s[ns * BM + row] = 0.f;               // "no bias"
-  table_s[(ns + 1) * BM + row] = -INFINITY;   // key past the sequence end
-}
-
-// Starts fetching into L2 the Look row that stage_table will read for query
-// token i of (b, h) in a later work item.
-__device__ __forceinline__ void prefetch_table_row(const TcArgs& a, int64_t b, int64_t h, int64_t i) {
-  const SlaParams& p = a.p;
-  if (!a.pose_vec4 || i < 1 || i >= p.seq) return;
-  const int64_t base = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
-  bulk_prefetch_l2(static_cast<const float*>(p.pose) + base, static_cast<uint32_t>(a.n_slots) * 4u);
-}
 
 // S row (64 fp32 scores of this thread's TMEM lane) into t[c] = keys 2c, 2c+1.
 __device__ __forceinline__ void load_s_row(uint32_t s_addr, float2 (&t)[BN / 2]) {
@@ -489,7 +273,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       bool ok = true;
       auto load_v = [&](int64_t jv, int32_t h, int32_t b) -> bool {
         const uint32_t vs = v_iter % kVStages, n = v_iter / kVStages;
-        if (n > 0 && !mbar_wait(&bars->v_empty[vs], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer))
+        if (n > 0 && !mbar_wait(&bars->v_empty[vs], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer, a.wait_ns))
           return false;
         mbar_arrive_expect_tx(&bars->v_full[vs], kKVBytes);
         const int32_t r = static_cast<int32_t>(jv * BN);
@@ -503,7 +287,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const uint32_t bh = item / n_qt;
         const int32_t h = static_cast<int32_t>(bh % H), b = static_cast<int32_t>(bh / H);
         if (item_iter > 0 && !mbar_wait(&bars->q_empty, (item_iter - 1) & 1, abort_flag, p.status,
-                                        kDevTimeoutProducer)) {
+                                        kDevTimeoutProducer, a.wait_ns)) {
           ok = false;
           break;
         }
@@ -515,7 +299,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         }
         for (int64_t j = 0; j < n_kt; ++j) {
           const uint32_t ks = k_iter % KS, n = k_iter / KS;
-          if (n > 0 && !mbar_wait(&bars->k_empty[ks], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer)) {
+          if (n > 0 && !mbar_wait(&bars->k_empty[ks], (n - 1) & 1, abort_flag, p.status, kDevTimeoutProducer, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -567,9 +351,9 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       // O += P [V | 1] for the tile whose P the softmax just published (global tile pv_iter).
       auto issue_pv = [&](bool first_tile) -> bool {
         const uint32_t pb = pv_iter & 1;
-        if (!mbar_wait(&bars->p_full[pb], (pv_iter >> 1) & 1, abort_flag, p.status, kDevTimeoutMma)) return false;
+        if (!mbar_wait(&bars->p_full[pb], (pv_iter >> 1) & 1, abort_flag, p.status, kDevTimeoutMma, a.wait_ns)) return false;
         const uint32_t vs = v_iter % kVStages;
-        if (!mbar_wait(&bars->v_full[vs], (v_iter / kVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
+        if (!mbar_wait(&bars->v_full[vs], (v_iter / kVStages) & 1, abort_flag, p.status, kDevTimeoutMma, a.wait_ns))
           return false;
         tc_fence_after();
         const uint64_t vd = vs == 0 ? v_desc0 : v_desc1;
@@ -584,21 +368,21 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         return true;
       };
       for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_iter) {
-        if (!mbar_wait(&bars->q_full, item_iter & 1, abort_flag, p.status, kDevTimeoutMma)) {
+        if (!mbar_wait(&bars->q_full, item_iter & 1, abort_flag, p.status, kDevTimeoutMma, a.wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int64_t j = 0; j < n_kt && ok; ++j) {
           const uint32_t ks = k_iter % KS;
-          if (!mbar_wait(&bars->k_full[ks], (k_iter / KS) & 1, abort_flag, p.status, kDevTimeoutMma)) {
+          if (!mbar_wait(&bars->k_full[ks], (k_iter / KS) & 1, abort_flag, p.status, kDevTimeoutMma, a.wait_ns)) {
             ok = false;
             break;
           }
           // S buffer sb last held P of tile s_iter - 2: its PV must be done.
           const uint32_t sb = s_iter & 1;
           if (s_iter >= 2 &&
-              !mbar_wait(&bars->pv_done[sb], ((s_iter - 2) >> 1) & 1, abort_flag, p.status, kDevTimeoutMma)) {
+              !mbar_wait(&bars->pv_done[sb], ((s_iter - 2) >> 1) & 1, abort_flag, p.status, kDevTimeoutMma, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -643,7 +427,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     uint32_t g = 0;  // global index of the key tile being processed (S/P buffer g & 1)
     // Waits until the PV MMA of global tile t (buffer t & 1) has completed.
     auto wait_pv = [&](uint32_t t) -> bool {
-      return mbar_wait(&bars->pv_done[t & 1], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax);
+      return mbar_wait(&bars->pv_done[t & 1], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns);
     };
     bool ok = true;
     // SLOT_FIELDS inputs of a work item are fetched one item ahead: the pose
@@ -659,17 +443,17 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       load_pose_row(w, a, ibh / H, ibh % H, static_cast<int64_t>(it % n_qt) * BM + row);
       if (!a.sf_vec4) return true;
       if (sf_count > 0 &&
-          !mbar_wait(&bars->sf_free, (sf_count - 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax))
+          !mbar_wait(&bars->sf_free, (sf_count - 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns))
         return false;
-      stage_slot_fields(table_s, a, ibh % H, row);
+      stage_slot_fields(table_s + a.sf_offset, a, ibh % H, row, BM);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->sf_ready);
       return true;
     };
     auto sf_finish = [&](int64_t head) -> bool {
-      if (a.sf_vec4 && !mbar_wait(&bars->sf_ready, sf_count & 1, abort_flag, p.status, kDevTimeoutSoftmax))
+      if (a.sf_vec4 && !mbar_wait(&bars->sf_ready, sf_count & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns))
         return false;
-      build_table_sf(table_s, a, head, row, w);
+      build_table_sf(table_s, table_s + a.sf_offset, a, head, row, w);
       if (a.sf_vec4) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->sf_free);
@@ -717,7 +501,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                       (static_cast<uint64_t>(__ballot_sync(0xffffffffu, (fl1 >> warp) & 1)) << 32);
         }
         const uint32_t sb = g & 1;
-        if (!mbar_wait(&bars->s_full[sb], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+        if (!mbar_wait(&bars->s_full[sb], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) {
           ok = false;
           break;
         }
@@ -731,7 +515,7 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const uint32_t st = k_iter % KS;
         const bool bias_tile = (tile_mask >> (j & 63)) & 1u;
         if (bias_tile) {
-          if (!mbar_wait(&bars->k_full[st], (k_iter / KS) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+          if (!mbar_wait(&bars->k_full[st], (k_iter / KS) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -851,58 +635,6 @@ sla_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------- host side
-EncodeTiledFn get_encode_fn() { return tensor_map_encoder(); }
-
-// Builds a 4-D map (head_dim, then row / head / batch sorted by stride) over a
-// (B, H, N, D) tensor with element strides `stride`, and reports where each
-// logical coordinate lands.  Box: 64 x box_rows x 1 x 1 with 128-byte swizzle.
-bool make_map(CUtensorMap* map, MapOrder* order, const void* base, const int64_t* stride, const SlaParams& p,
-              uint32_t box_rows) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return false;
-  const CUtensorMapDataType dt = p.dtype == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  // logical outer dims: 0 = row (seq), 1 = head, 2 = batch
-  const int64_t ext[3] = {p.seq, p.heads, p.batch};
-  const int64_t str[3] = {stride[2], stride[1], stride[0]};
-  const uint32_t bx[3] = {box_rows, 1, 1};
-  int idx[3] = {0, 1, 2};
-  for (int x = 0; x < 3; ++x)
-    for (int y = x + 1; y < 3; ++y)
-      if (str[idx[y]] < str[idx[x]] || (str[idx[y]] == str[idx[x]] && idx[y] < idx[x])) {
-        const int tmp = idx[x];
-        idx[x] = idx[y];
-        idx[y] = tmp;
-      }
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.head_dim), 0, 0, 0};
-  cuuint64_t strides[3];
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(HD), 1, 1, 1};
-  int8_t pos[3];
-  for (int x = 0; x < 3; ++x) {
-    dims[x + 1] = static_cast<cuuint64_t>(ext[idx[x]]);
-    strides[x] = static_cast<cuuint64_t>(str[idx[x]]) * 2;
-    box[x + 1] = bx[idx[x]];
-    pos[idx[x]] = static_cast<int8_t>(x + 1);
-  }
-  order->row = pos[0];
-  order->head = pos[1];
-  order->batch = pos[2];
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  return enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-bool tma_stride_ok(const void* base, const int64_t* stride) {
-  if (reinterpret_cast<uintptr_t>(base) % 16) return false;
-  if (stride[3] != 1) return false;
-  for (int d = 0; d < 3; ++d) {
-    if (stride[d] <= 0) return false;
-    if ((stride[d] * 2) % 16) return false;
-    if (stride[d] * 2 >= (int64_t(1) << 40)) return false;
-  }
-  return true;
-}
-
 uint32_t table_bytes_for(int32_t n_slots) {
   return n_slots > 0 ? static_cast<uint32_t>((n_slots + 2) * BM * sizeof(float)) : 0u;
 }
@@ -970,12 +702,14 @@ int32_t sla_tc_supported(const SlaParams& p) {
 
 int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
   if (!sla_tc_supported(p)) return 8;
+  if (sla_short_supported(p)) return launch_sla_short(p, stream, sm_count);  // N <= 256: one pass per row
   CUtensorMap mq, mk, mv;
   TcArgs a;
   if (!make_map(&mq, &a.oq, p.q, p.q_stride, p, BM) || !make_map(&mk, &a.ok, p.k, p.k_stride, p, BN) ||
       !make_map(&mv, &a.ov, p.v, p.v_stride, p, BN))
     return 4;
   a.p = p;
+  a.wait_ns = tc_wait_budget_ns();
   a.n_qt = (p.seq + BM - 1) / BM;
   a.n_kt = (p.seq + BN - 1) / BN;
   a.n_items = p.batch * p.heads * a.n_qt;

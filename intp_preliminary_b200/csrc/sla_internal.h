@@ -54,6 +54,10 @@ int32_t launch_nl1_backward(const float* x, const float* w, const float* grad_ou
 // Returns INTP_ERR_UNSUPPORTED (8) when the tensor-core path does not apply.
 int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count);
 int32_t sla_tc_supported(const SlaParams& p);
+// The single-pass tensor-core kernel for sequences of at most 256 tokens
+// (look_attention_short.cu); launch_sla_tc dispatches to it when it applies.
+int32_t sla_short_supported(const SlaParams& p);
+int32_t launch_sla_short(const SlaParams& p, cudaStream_t stream, int sm_count);
 int32_t launch_nl1(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
                    cudaStream_t stream);
 

@@ -98,14 +98,37 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // of the CTA already gave up); on timeout it raises *abort and records `code`.
 // Waiting threads sleep inside try_wait (suspend hint) and look at the clock
 // and the abort flag only between sleeps, so a wait costs few issue slots.
+// `budget_ns` shortens the budget of pipeline waits (a launch parameter of the
+// tensor-core kernels); waits that drain in-flight copies and MMAs keep the default.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
-                                          int32_t* status, int32_t code) {
+                                          int32_t* status, int32_t code, uint64_t budget_ns = kWaitBudgetNs) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  // Suspend at most the budget per try (a short budget must be able to expire).
+  const uint32_t hint = budget_ns < 200000ull ? static_cast<uint32_t>(budget_ns) : 200000u;
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
+    if (*abort) return false;
+    if (global_ns() - start > budget_ns) {
+      *abort = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
+// mbar_wait without the suspend hint: the thread retries try_wait (which
+// blocks in hardware for a short, system-defined time) and resumes as soon as
+// the phase completes.  For single issuing threads on a critical path, where a
+// late wake-up costs more than the retries.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
+                                               int32_t* status, int32_t code, uint64_t budget_ns = kWaitBudgetNs) {
   if (mbar_test_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_ns() - start > kWaitBudgetNs) {
+    if (global_ns() - start > budget_ns) {
       *abort = 1;
       if (status) atomicCAS(status, 0, code);
       return false;
@@ -225,6 +248,14 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
       "{%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
+}
+
+// 32 lanes x 32-bit, 2 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t (&r)[2]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, const uint32_t (&r)[2]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(r[0]), "r"(r[1]) : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
