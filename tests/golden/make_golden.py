@@ -1,8 +1,8 @@
 """Generate the golden fixtures of tests/golden/ by running the REFERENCE code.
 
 This script imports the reference's own Python modules (it must run where the
-reference checkout is available, passed as --reference, default
-/root/reference) and records their outputs on seeded inputs:
+reference checkout is available; its path is the required --reference
+argument) and records their outputs on seeded inputs:
 
   look_attention_reference.npz
       ``reference_structured_look_attention`` (layers/triton_structured_look_attention.py:25-54)
@@ -13,7 +13,7 @@ reference checkout is available, passed as --reference, default
       one-hot fields.
   negative_l1_reference.npz
       ``negative_l1_distance`` CPU path (layers/triton_negative_l1.py:233-241) on the
-      reference test shapes and a small slice of the BASELINE shapes.
+      reference test shapes and a small slice of the 50176 x 576 x {1728, 432} shapes.
   hex_bins_reference.npz
       ``hex_relative_bins`` (utils/hex_graph.py:25-47) on the synthetic
       14x14 lattice and on the real half6d3r tokenizer lattice (195 patches).
@@ -116,7 +116,7 @@ def _dense_look_grid() -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of the reference checkout")
     parser.add_argument("--only", choices=("all", "dense_look_grid"), default="all")
     args = parser.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))

@@ -2,7 +2,7 @@
 the reference's golden outputs.  Every call goes through libintp_b200.so.
 
 Tolerances: the reference's own (fp32 2e-5, fp16 2e-3, tests/test_triton_structured_look_attention.py:60-141)
-where its inputs are replayed; BASELINE's (fp32 1e-4 max-abs, bf16 2e-2 max-abs) for
+where its inputs are replayed; fp32 1e-4 max-abs and bf16 2e-2 max-abs for
 the synthetic Look configurations, with tighter internal bars where they hold.
 """
 
@@ -52,7 +52,7 @@ def test_reference_inputs_fp16(cuda_device, poses):
 
 
 def test_config1_fp32_slots_and_fields(cuda_device):
-    """14x14 hex lattice, 12 directions x 4 rings, fp32 (BASELINE config 1 shape, B=1)."""
+    """14x14 hex lattice, 12 directions x 4 rings, fp32 (the B8 H3 N197 Look layer's lattice, B=1)."""
     g = _case("cfg1")
     q, k, v, pose = (tensor(g[n]).to(cuda_device) for n in ("q", "k", "v", "pose"))
     slots = LookSlots(g["slots"], int(g["n_slots"]))
@@ -143,7 +143,7 @@ def test_strided_qkv_view(cuda_device):
 
 
 def test_config4_full_size_properties(cuda_device):
-    """BASELINE config 4 at full size (B64, H6, N1025, bf16): oracle on a sampled
+    """The long-sequence Look layer at full size (B64, H6, N1025, bf16): oracle on a sampled
     subset of (batch, head) pairs, finiteness and run-to-run determinism."""
     batch, heads, rows, cols = 64, 6, 32, 32
     q, k, v, pose, slots = _random_slot_inputs(batch, heads, rows, cols, 8, 4, torch.bfloat16, cuda_device, seed=7)

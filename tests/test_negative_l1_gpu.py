@@ -58,7 +58,7 @@ def test_noncontiguous_and_half_inputs_are_converted(cuda_device):
 
 
 def test_full_baseline_shape_properties(cuda_device):
-    """BASELINE config 3 at full size (M = 256*196, P = 576, F = 1728): sampled
+    """The standalone projection at full size (M = 256*196, P = 576, F = 1728): sampled
     rows against the oracle, the identity d(w_p, w_p) = 0, and non-positivity."""
     g = torch.Generator(device=cuda_device).manual_seed(0)
     rows, protos, features = 256 * 196, 576, 1728

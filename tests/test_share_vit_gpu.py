@@ -30,13 +30,48 @@ def test_fp32_forward_matches_reference(cuda_device):
 
 
 def test_bf16_forward_tracks_reference(cuda_device):
-    """bf16 GEMMs + tensor-core Look attention vs the fp32 reference."""
+    """bf16 GEMMs + tensor-core Look attention vs the fp32 reference logits.
+
+    The bar is derived from the reference's own algorithm with bf16-rounded
+    operands: the fp32 oracle forward (oracle/share_vit_cpu.py) run with every
+    weight matrix rounded to bf16 lands 4.0e-3 from the fp32 logits on these
+    inputs (logits up to 0.78); 4x that covers the activation roundings the
+    bf16 trunk adds."""
     logits = _model("bf16", cuda_device)(_images(cuda_device)).float().cpu().numpy()
     check_device_status(cuda_device)
     ref = GOLD["logits"]
-    err = np.abs(logits - ref).max()
-    assert err <= 0.05 * np.abs(ref).max(), err
-    assert np.corrcoef(logits.ravel(), ref.ravel())[0, 1] > 0.999
+    err = float(np.abs(logits - ref).max())
+    assert err <= 1.6e-2, err
+
+
+def test_in_model_attention_full_size_vs_oracle(cuda_device):
+    """One layer's attention at the model's full size (B256 H3 N196, SLOT_FIELDS
+    with the layer's own pose and slot values) against the float64 oracle on
+    sampled (batch, head) pairs, at the 2e-2 bf16 bar."""
+    from intp_preliminary_b200.look_attention import look_attention_forward
+    from oracle.look_attention import slot_look_attention_np
+
+    model = _model("bf16", cuda_device)
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    images = torch.randn(256, 3, 224, 224, device=cuda_device, generator=g)
+    inputs = []
+    model.attention_inputs = inputs
+    with torch.no_grad():
+        model(images)
+    model.attention_inputs = None
+    for layer in (0, 11):
+        q, k, v, pose, fields, scale = inputs[layer]
+        out, _ = look_attention_forward(q, k, v, pose, fields, scale=scale)
+        check_device_status(cuda_device)
+        per_slot = torch.einsum("bqhp,hps->bqhs", pose.float(), fields.values.float())
+        for b, h in ((0, 0), (97, 1), (255, 2)):
+            exact = slot_look_attention_np(q[b:b + 1, h:h + 1].float().cpu().numpy(),
+                                           k[b:b + 1, h:h + 1].float().cpu().numpy(),
+                                           v[b:b + 1, h:h + 1].float().cpu().numpy(),
+                                           per_slot[b:b + 1, :, h:h + 1].cpu().numpy(), fields.slots.table,
+                                           scale=scale)
+            err = float(np.abs(out[b:b + 1, h:h + 1].float().cpu().numpy() - exact).max())
+            assert err <= 2e-2, (layer, b, h, err)
 
 
 def test_bf16_batch_forward_is_finite_and_batch_consistent(cuda_device):
