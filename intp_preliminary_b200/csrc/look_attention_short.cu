@@ -48,6 +48,7 @@ constexpr int QM = 128;                       // query rows per tile
 constexpr int SHD = 64;                       // head_dim
 constexpr int kShortThreads = 512;
 constexpr int kMaxShortSeq = 256;
+constexpr int kMaxShortFieldPoses = 64;       // FIELDS: poses summed per key in pass 1
 constexpr uint32_t kQTile = QM * SHD * 2;     // 16 KB
 constexpr uint32_t kPackedTile = kSlotTileBytes;  // 8 KB packed pair tile (128 q x 64 k)
 
@@ -77,6 +78,7 @@ struct ShortArgs {
   int32_t n_kt;           // 64-key tiles of the packed pair table
   int32_t n_slots;        // 0: no Look bias
   int32_t slot_fields, n_poses, pose_vec4, sf_vec4;
+  int32_t fields_mode;    // FIELDS: the general (H, P, Np, Np) fields, summed per key in pass 1
   uint32_t off_k, off_v, off_slots, off_table, off_sf, off_bars;  // smem offsets
   uint32_t sf_floats;     // SLOT_FIELDS: floats of one staging buffer (n_poses * n_slots)
   uint32_t table_floats;  // per tile: (n_slots + 2) * 128
@@ -162,7 +164,63 @@ __device__ __forceinline__ float chunk_logits(float2 (&t)[16], float scale_log2,
   return fmax3s(fmax3s(m4[0], m4[1], m), m4[2], m4[3]);
 }
 
-template <bool BF16>
+// Running row max over a 32-key chunk of logits.
+__device__ __forceinline__ float row_max32(const float2 (&t)[16], float m) {
+  float m4[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2* v = t + 4 * k;
+    m4[k] = fmaxf(fmax3s(fmax3s(v[0].x, v[0].y, v[1].x), fmax3s(v[1].y, v[2].x, v[2].y), v[3].x), v[3].y);
+  }
+  return fmax3s(fmax3s(m4[0], m4[1], m), m4[2], m4[3]);
+}
+
+// The general Look terms of the reference's form for query token i and key
+// tokens c0 .. c0+nk-1 (log2 domain, added to t): the dense bias
+// dense[b, h, i-1, j-1] and the FIELDS bias sum_p pose[b, i-1, h, p] *
+// fields[h, p, i-1, j-1] (layers/triton_structured_look_attention.py:116-139);
+// the CLS token (0) and keys past the sequence get neither.
+template <class A>
+__device__ __forceinline__ void add_general_bias(float2 (&t)[16], const A& a, uint32_t item, int32_t i, int c0,
+                                                 int nk) {
+  const SlaParams& p = a.p;
+  const int32_t N = static_cast<int32_t>(p.seq);
+  if (i < 1 || i >= N) return;
+  const int64_t h = item % static_cast<uint32_t>(p.heads), b = item / static_cast<uint32_t>(p.heads);
+  float add[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) add[e] = 0.f;
+  if (p.dense != nullptr) {
+    const int64_t base = b * p.dense_stride[0] + h * p.dense_stride[1] + (i - 1) * p.dense_stride[2];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int32_t j = c0 + e;
+      if (e < nk && j >= 1 && j < N) add[e] = load_any(p.dense, base + (j - 1) * p.dense_stride[3], p.dense_dtype);
+    }
+  }
+  if (a.fields_mode) {
+    const int64_t pbase = b * p.pose_stride[0] + (i - 1) * p.pose_stride[1] + h * p.pose_stride[2];
+    for (int pp = 0; pp < a.n_poses; ++pp) {
+      const float w = load_any(p.pose, pbase + pp * p.pose_stride[3], p.pose_dtype);
+      const int64_t fbase = h * p.fields_stride[0] + pp * p.fields_stride[1] + (i - 1) * p.fields_stride[2];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int32_t j = c0 + e;
+        if (e < nk && j >= 1 && j < N)
+          add[e] = fmaf(w, load_any(p.fields, fbase + (j - 1) * p.fields_stride[3], p.fields_dtype), add[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    t[e].x = fmaf(add[2 * e], kLog2eF, t[e].x);
+    t[e].y = fmaf(add[2 * e + 1], kLog2eF, t[e].y);
+  }
+}
+
+// GENERAL: the dense-bias / general-fields terms are compiled in (a separate
+// instance, so the SLOTS / SLOT_FIELDS / no-bias path carries no code for them).
+template <bool BF16, bool GENERAL>
 __global__ void __launch_bounds__(kShortThreads, 1)
 sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const ShortArgs a) {
@@ -324,6 +382,7 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const float scale_log2 = p.scale * kLog2eF;
     const int32_t tok = x * QM + row;
     const bool warp_live = x < nt && x * QM + qw * 32 < N;  // some row of this warp is a token
+    constexpr bool general = GENERAL;
     float* trow = table_s + x * a.table_floats + row;
     const uint8_t* srow = slots_s + static_cast<uint32_t>(x * a.n_kt) * kPackedTile + row * 16;
     // Per 64-key tile of the pair table: does this warp's block carry Look bias
@@ -383,6 +442,7 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           } else {
             ld32(lane_base + c0, t);
           }
+          if constexpr (!general) {
           const int kt = c0 >> 6;
           const bool bias = (bias_tiles >> kt) & 1u;
           const uint8_t* sb = srow + kt * kPackedTile + ((c0 & 63) >> 4) * 2048;
@@ -401,6 +461,42 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             for (int e = 0; e < 8; ++e) m = fmax3s(m, t[e].x, t[e].y);
           } else {
             m = chunk_logits(t, scale_log2, bias, sb, trow, !use_bias && c0 + 32 > N, N - c0, m);
+          }
+          } else {
+          const int kt = c0 >> 6;
+          const bool bias = (bias_tiles >> kt) & 1u;
+          const uint8_t* sb = srow + kt * kPackedTile + ((c0 & 63) >> 4) * 2048;
+          if (bias) {
+            // logits = scale log2(e) s + table[slot]; a 16-key tail reads 16 slot bytes
+            const uint4 w0 = *reinterpret_cast<const uint4*>(sb);
+            const uint4 w1 = half ? make_uint4(0u, 0u, 0u, 0u) : *reinterpret_cast<const uint4*>(sb + 2048);
+            const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const uint32_t s0 = __byte_perm(ww[e >> 2], 0u, 0x4440u | (e & 3));
+              const uint32_t s1 = __byte_perm(ww[e >> 2], 0u, 0x4440u | ((e + 1) & 3));
+              t[e / 2].x = fmaf(t[e / 2].x, scale_log2, trow[s0 * kTableRows]);
+              t[e / 2].y = fmaf(t[e / 2].y, scale_log2, trow[s1 * kTableRows]);
+            }
+          } else {
+            const float2 c2 = make_float2(scale_log2, scale_log2);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) t[e] = mul2(t[e], c2);
+          }
+          if constexpr (general) add_general_bias(t, a, item, tok, c0, half ? 16 : 32);
+          if (!use_bias && c0 + 32 > N) {
+            // no pair table marks the keys past the end: mask them here
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              if (c0 + 2 * e >= N) t[e].x = -INFINITY;
+              if (c0 + 2 * e + 1 >= N) t[e].y = -INFINITY;
+            }
+          }
+          if (half) {
+#pragma unroll
+            for (int e = 8; e < 16; ++e) t[e] = make_float2(-INFINITY, -INFINITY);
+          }
+          m = row_max32(t, m);
           }
           if (half) {
             uint32_t r0[16];
@@ -564,7 +660,22 @@ uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 int32_t sla_short_supported(const SlaParams& p) {
   if (p.seq < 2 || p.seq > kMaxShortSeq) return 0;
-  if (!sla_tc_supported(p)) return 0;
+  if (!tc_common_ok(p)) return 0;
+  switch (p.bias_mode) {
+    case 0: break;
+    case 1:
+      if (!p.pose || !p.fields || p.poses < 1 || p.poses > kMaxShortFieldPoses) return 0;
+      break;
+    case 2:
+      if (p.poses < 1 || p.poses > kMaxLookSlots || !p.slots_packed || !p.slot_tile_flags) return 0;
+      break;
+    case 3:
+      if (p.slots < 1 || p.slots > kMaxLookSlots || p.poses < 1 || p.poses > kMaxLookPoses || !p.slots_packed ||
+          !p.slot_tile_flags || !p.fields)
+        return 0;
+      break;
+    default: return 0;
+  }
   const int32_t n_slots =
       p.bias_mode == 2 ? static_cast<int32_t>(p.poses) : (p.bias_mode == 3 ? static_cast<int32_t>(p.slots) : 0);
   const int64_t kr = (p.seq + 15) / 16 * 16;
@@ -598,7 +709,8 @@ int32_t launch_sla_short(const SlaParams& p, cudaStream_t stream, int sm_count) 
   a.n_kt = static_cast<int32_t>((p.seq + kSlotTileK - 1) / kSlotTileK);
   a.n_slots = p.bias_mode == 2 ? static_cast<int32_t>(p.poses) : (p.bias_mode == 3 ? static_cast<int32_t>(p.slots) : 0);
   a.slot_fields = p.bias_mode == 3 ? 1 : 0;
-  a.n_poses = p.bias_mode == 3 ? static_cast<int32_t>(p.poses) : 0;
+  a.fields_mode = p.bias_mode == 1 ? 1 : 0;
+  a.n_poses = (p.bias_mode == 3 || p.bias_mode == 1) ? static_cast<int32_t>(p.poses) : 0;
   a.sf_vec4 = (p.bias_mode == 3 && p.fields_dtype == 0 && p.fields_stride[2] == 1 && a.n_slots % 4 == 0 &&
                reinterpret_cast<uintptr_t>(p.fields) % 16 == 0 && p.fields_stride[0] % 4 == 0 &&
                p.fields_stride[1] % 4 == 0)
@@ -627,7 +739,9 @@ int32_t launch_sla_short(const SlaParams& p, cudaStream_t stream, int sm_count) 
   size_t smem = a.off_bars + sizeof(ShortBars) + 1024;
   if (smem < 120 * 1024) smem = 120 * 1024;
   a.wait_ns = tc_wait_budget_ns();
-  auto kernel = p.dtype == 2 ? sla_short_kernel<true> : sla_short_kernel<false>;
+  const bool general = a.fields_mode || p.dense != nullptr;
+  auto kernel = p.dtype == 2 ? (general ? sla_short_kernel<true, true> : sla_short_kernel<true, false>)
+                             : (general ? sla_short_kernel<false, true> : sla_short_kernel<false, false>);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return 6;
   int64_t grid = sm_count;

@@ -677,15 +677,11 @@ int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
 
 }  // namespace
 
-int32_t sla_tc_supported(const SlaParams& p) {
+// What both tensor-core kernels need: 16-bit q / k / v / out with head_dim 64
+// in layouts TMA can read, a status word, sane sizes and scale.
+int32_t tc_common_ok(const SlaParams& p) {
   if (p.dtype != 1 && p.dtype != 2) return 0;
   if (p.head_dim != HD) return 0;
-  if (p.dense != nullptr) return 0;
-  if (p.bias_mode != 0 && p.bias_mode != 2 && p.bias_mode != 3) return 0;
-  if (p.bias_mode == 2 && (p.poses < 1 || p.poses > kMaxSlots || !p.slots_packed || !p.slot_tile_flags)) return 0;
-  if (p.bias_mode == 3 && (p.slots < 1 || p.slots > kMaxSlots || p.poses < 1 || p.poses > kMaxPoses ||
-                           !p.slots_packed || !p.slot_tile_flags || !p.fields))
-    return 0;
   if (p.status == nullptr) return 0;
   if (p.seq < 2 || p.seq > (int64_t(1) << 30) || p.batch > (int64_t(1) << 30) || p.heads > (int64_t(1) << 30))
     return 0;
@@ -700,9 +696,23 @@ int32_t sla_tc_supported(const SlaParams& p) {
   return 1;
 }
 
+// The tiled kernel (any N): no bias, SLOTS or SLOT_FIELDS, no dense bias.
+int32_t sla_long_supported(const SlaParams& p) {
+  if (!tc_common_ok(p)) return 0;
+  if (p.dense != nullptr) return 0;
+  if (p.bias_mode != 0 && p.bias_mode != 2 && p.bias_mode != 3) return 0;
+  if (p.bias_mode == 2 && (p.poses < 1 || p.poses > kMaxSlots || !p.slots_packed || !p.slot_tile_flags)) return 0;
+  if (p.bias_mode == 3 && (p.slots < 1 || p.slots > kMaxSlots || p.poses < 1 || p.poses > kMaxPoses ||
+                           !p.slots_packed || !p.slot_tile_flags || !p.fields))
+    return 0;
+  return 1;
+}
+
+int32_t sla_tc_supported(const SlaParams& p) { return sla_short_supported(p) || sla_long_supported(p) ? 1 : 0; }
+
 int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count) {
-  if (!sla_tc_supported(p)) return 8;
   if (sla_short_supported(p)) return launch_sla_short(p, stream, sm_count);  // N <= 256: one pass per row
+  if (!sla_long_supported(p)) return 8;
   CUtensorMap mq, mk, mv;
   TcArgs a;
   if (!make_map(&mq, &a.oq, p.q, p.q_stride, p, BM) || !make_map(&mk, &a.ok, p.k, p.k_stride, p, BN) ||

@@ -53,9 +53,15 @@ int32_t launch_nl1_backward(const float* x, const float* w, const float* grad_ou
                             int64_t rows, int64_t protos, int64_t features, cudaStream_t stream);
 // Returns INTP_ERR_UNSUPPORTED (8) when the tensor-core path does not apply.
 int32_t launch_sla_tc(const SlaParams& p, cudaStream_t stream, int sm_count);
+// 1 when one of the two tensor-core kernels takes the request.
 int32_t sla_tc_supported(const SlaParams& p);
+// Requirements both tensor-core kernels share (look_attention_tc.cu).
+int32_t tc_common_ok(const SlaParams& p);
+// The tiled tensor-core kernel (any N; no dense bias, no general fields).
+int32_t sla_long_supported(const SlaParams& p);
 // The single-pass tensor-core kernel for sequences of at most 256 tokens
-// (look_attention_short.cu); launch_sla_tc dispatches to it when it applies.
+// (look_attention_short.cu, every bias mode and dense bias); launch_sla_tc
+// prefers it when it applies.
 int32_t sla_short_supported(const SlaParams& p);
 int32_t launch_sla_short(const SlaParams& p, cudaStream_t stream, int sm_count);
 int32_t launch_nl1(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,

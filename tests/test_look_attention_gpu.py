@@ -202,3 +202,27 @@ def test_empty_batch(cuda_device):
     out = structured_look_attention(q, q, q, torch.zeros(0, 8, 2, 4, device=cuda_device),
                                     torch.zeros(2, 4, 8, 8, device=cuda_device), scale=0.125)
     assert out.shape == q.shape
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("patches,poses,dense", [(40, 12, True), (40, 18, False), (129, 1, True), (195, 18, True),
+                                                 (255, 6, False), (5, 3, True)])
+def test_tcgen05_general_fields_and_dense_vs_oracle(cuda_device, dtype, patches, poses, dense):
+    """The reference's general form - dense (H, P, Np, Np) fields and a dense
+    (B, H, Np, Np) bias, as the dual-Look model (P = 12 + 6) and the grid-first
+    variants pass them - on the tensor-core kernel (N <= 256)."""
+    g = torch.Generator().manual_seed(patches * 7 + poses)
+    batch, heads = 2, 3
+    q, k, v = ((torch.randn(batch, heads, patches + 1, 64, generator=g) / 8).to(dtype) for _ in range(3))
+    pose = torch.rand(batch, patches, heads, poses, generator=g)
+    fields = torch.randn(heads, poses, patches, patches, generator=g) * 0.3
+    dense_t = torch.randn(batch, heads, patches, patches, generator=g) * 0.3 if dense else None
+    out, lse = look_attention_forward(*(t.to(cuda_device) for t in (q, k, v, pose, fields)), scale=0.125,
+                                      dense_bias=dense_t.to(cuda_device) if dense else None, kernel="tcgen05",
+                                      want_lse=True)
+    exact, exact_lse = look_attention_np(q.float().numpy(), k.float().numpy(), v.float().numpy(), pose.numpy(),
+                                         fields.numpy(), scale=0.125,
+                                         dense_bias=dense_t.numpy() if dense else None, return_lse=True)
+    err = np.abs(out.float().cpu().numpy() - exact).max()
+    assert err <= (8e-3 if dtype == torch.bfloat16 else 2e-3), err
+    assert np.abs(lse.cpu().numpy() - exact_lse).max() <= 1e-3
