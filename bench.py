@@ -626,6 +626,63 @@ def _look_roofline(flops: float, per_launch_ms: float, peaks: dict, traffic, ker
             "launch_ms": round(per_launch_ms, 5), "where": where}
 
 
+def _nl1_roofline(work, per_launch_ms: float, peaks: dict) -> dict:
+    """negative-L1: GB/s against HBM as asked, and beside it the op rate
+    against the FP32 lanes' rate at the maximum SM clock (148 SMs x 128
+    lanes; one lane-op per counted op) - the kernel is FP32-pipe bound."""
+    gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
+    fp32_peak = 148 * 128 * 1.965e9 / 1e12
+    tops = work.flops / (per_launch_ms * 1e-3) / 1e12
+    return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": NL1_TRAFFIC_BYTES.get(work.features),
+            "kernel": "nl1_vec_kernel", "peak_source": f"{peaks['source']} HBM copy bandwidth",
+            "launch_ms": round(per_launch_ms, 5),
+            "note": "FP32-pipe bound; fp32_tops / fp32_peak_tops is the binding fraction",
+            "fp32_tops": round(tops, 2), "fp32_peak_tops": round(fp32_peak, 1), "fp32_frac": round(tops / fp32_peak, 4)}
+
+
+def _side_line(work, args, ctx, flush, roofline_fn) -> dict:
+    """Device rate, roofline, end-to-end rate and CPU baseline of a workload
+    timed beside the model (the same timing rules as the main line)."""
+    from intp_preliminary_b200.sharding import max_over_ranks
+
+    steps = max(args.steps, 5)
+    times = _timed_steps(work.step, steps, args.warmup, ctx, flush)
+    ms = max_over_ranks(statistics.mean(times), ctx)
+    line = {"config": work.config, "metric": work.metric, "unit": work.unit,
+            "value": round(work.units_per_step / (ms * 1e-3), 4), "ms_per_step": round(ms, 5),
+            "roofline": roofline_fn(ms)}
+    host_inputs, host_out = work.e2e_inputs(), work.e2e_output()
+    e2e_times = _timed_steps(lambda: work.e2e_step(host_inputs, host_out), steps, args.warmup, ctx, flush)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), ctx)
+    line["e2e"] = {"value": round(work.units_per_step / (e2e_ms * 1e-3), 4), "unit": work.unit,
+                   "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_inputs),
+                   "d2h_bytes_per_step": host_out.numel() * host_out.element_size()}
+    if ctx.is_main and not args.no_cpu_baseline:
+        result = work.cpu_reference()
+        line["cpu_baseline"] = {"value": round(result[0], 6), "unit": work.unit, "cores": torch.get_num_threads(),
+                                "kind": result[2] if len(result) > 2 else "port", "sample": result[1]}
+    return line
+
+
+def _reference_model_line(args, ctx, flush):
+    """`bench.py --workload reference_model` (the reference's own half6d3r
+    model code from baseline/_ref, unchanged, on this package's operators) in a
+    child process - its imports replace the reference's operator modules, which
+    this process's CPU baseline still needs.  One GPU runs only."""
+    if ctx.world != 1 or not (REFERENCE_DIR / "model" / "deit_tiny_rot_hex_look.py").exists():
+        return None
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--workload", "reference_model", "--steps", str(max(args.steps, 5)),
+           "--warmup", str(args.warmup), "--no-cpu-baseline"]
+    run = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    lines = [l for l in run.stdout.splitlines() if l.startswith("{")]
+    if run.returncode != 0 or not lines:
+        return {"unavailable": f"reference_model run failed (rc {run.returncode})"}
+    child = json.loads(lines[-1])
+    return {key: child[key] for key in ("metric", "value", "unit", "ms_per_step", "config", "e2e", "clocks",
+                                         "look_registry_hits_per_step") if key in child}
+
+
 def run_ours(args) -> None:
     from intp_preliminary_b200 import check_device_status
     from intp_preliminary_b200.sharding import barrier, init_from_env, max_over_ranks, shutdown
@@ -689,14 +746,30 @@ def run_ours(args) -> None:
         # qkv, Look attention, proj + residual + LN, fc1 + GELU, fc2 + residual + LN
         # (the tokenizer GEMM and the classifier head are cuBLAS)
         launches = (3 + 12 * 5) * args.steps
-        # the long-sequence Look layer (B64 H6 N1025) on its own
-        cfg4 = LookWorkload("look_cfg4", device, seed=99 + ctx.rank)
-        cfg4_times = _timed_steps(cfg4.step, max(args.steps, 5), args.warmup, ctx, flush)
-        cfg4_ms = max_over_ranks(statistics.mean(cfg4_times), ctx)
-        extra["look_attention_cfg4"] = {
-            "config": cfg4.config["workload"], "tflops": round(cfg4.flops / (cfg4_ms * 1e-3) / 1e12, 2),
-            "roofline": _look_roofline(cfg4.flops, cfg4_ms, peaks, CFG4_TRAFFIC_BYTES, "sla_tc_kernel",
-                                       "B64 H6 N1025 Look layer timed alone, one launch per step")}
+        # The other workloads of the hot path, each with its own device rate,
+        # roofline, end-to-end rate (host buffers) and CPU baseline: the
+        # long-sequence Look layer (B64 H6 N1025 bf16), the B8 H3 N197 fp32
+        # Look layer, the standalone negative-L1 projection, and the
+        # reference's own model code on this package's operators.
+        if not args.no_side:
+            cfg4 = LookWorkload("look_cfg4", device, seed=99 + ctx.rank, world=ctx.world)
+            extra["look_attention_cfg4"] = _side_line(
+                cfg4, args, ctx, flush, lambda ms: _look_roofline(
+                    cfg4.flops, ms, peaks, CFG4_TRAFFIC_BYTES, "sla_tc_kernel",
+                    "B64 H6 N1025 Look layer timed alone, one launch per step"))
+            cfg1 = LookWorkload("look_cfg1", device, seed=98 + ctx.rank, world=ctx.world)
+            extra["look_attention_cfg1"] = _side_line(
+                cfg1, args, ctx, flush, lambda ms: {
+                    **_look_roofline(cfg1.flops, ms, peaks, None, "sla_simt_kernel",
+                                     "B8 H3 N197 fp32 Look layer timed alone (CUDA-core fp32 kernel)"),
+                    "note": "fp32 correctness path on CUDA cores; the bf16 tensor peak is context only"})
+            nl1 = NegativeL1Workload(device, seed=97 + ctx.rank, world=ctx.world)
+            extra["negative_l1"] = _side_line(nl1, args, ctx, flush, lambda ms: _nl1_roofline(nl1, ms, peaks))
+            if ctx.is_main:
+                torch.cuda.synchronize(device)
+                ref_model = _reference_model_line(args, ctx, flush)
+                if ref_model is not None:
+                    extra["reference_model"] = ref_model
         extra["model_flops_per_image"] = MODEL_FLOPS_PER_IMAGE
         extra["model_tflops"] = round(value * MODEL_FLOPS_PER_IMAGE / 1e12, 2)
     elif isinstance(work, LookWorkload):
@@ -727,17 +800,7 @@ def run_ours(args) -> None:
         launches = args.steps
     else:
         gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
-        # The kernel is FP32-pipe bound (~214 ops per byte): GB/s against HBM as
-        # asked, and beside it the op rate against the FP32 lanes' rate at the
-        # maximum SM clock (148 SMs x 128 lanes; one lane-op per counted op).
-        fp32_peak = 148 * 128 * 1.965e9 / 1e12
-        tops = work.flops / (per_launch_ms * 1e-3) / 1e12
-        roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": NL1_TRAFFIC_BYTES.get(work.features),
-                    "kernel": "nl1_vec_kernel", "peak_source": f"{peaks['source']} HBM copy bandwidth",
-                    "note": "FP32-pipe bound; fp32_tops / fp32_peak_tops is the binding fraction",
-                    "fp32_tops": round(tops, 2), "fp32_peak_tops": round(fp32_peak, 1),
-                    "fp32_frac": round(tops / fp32_peak, 4)}
+        roofline = _nl1_roofline(work, per_launch_ms, peaks)
         launches = args.steps
         work.backward_prepare(77 + ctx.rank)
         bwd_ms = max_over_ranks(statistics.mean(_timed_steps(work.backward_step, args.steps, args.warmup, ctx,
@@ -915,6 +978,9 @@ def main() -> None:
                         help="total images over all GPUs (model workloads, strong scaling)")
     parser.add_argument("--features", type=int, default=1728, help="negative_l1 feature size F")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-side", action="store_true",
+                        help="model workload: skip the side lines (long Look layer, fp32 Look layer, "
+                             "negative-L1, reference model code)")
     args = parser.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
