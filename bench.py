@@ -378,11 +378,11 @@ class LookWorkload:
         g = torch.Generator(device=self.device).manual_seed(seed)
         self.grad_out = torch.randn(self.q.shape, device=self.device, generator=g).to(self.dtype)
 
-    def backward_step(self):
+    def backward_step(self, kernel: str = "auto"):
         from intp_preliminary_b200 import look_attention_backward
 
         look_attention_backward(self.q, self.k, self.v, self.bwd_out, self.bwd_lse, self.grad_out, self.pose,
-                                self.slots, scale=self.scale)
+                                self.slots, scale=self.scale, kernel=kernel)
 
     def e2e_inputs(self):
         return [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.pose)]
@@ -778,15 +778,21 @@ def run_ours(args) -> None:
                                   "sla_tc_kernel" if work.dtype != torch.float32 else "sla_simt_kernel",
                                   "one launch per timed step")
         launches = args.steps
-        # the CUDA-core backward (delta, rows and cols kernels) on the same inputs
+        # the backward on the same inputs: the tensor-core pass (16-bit inputs)
+        # and the CUDA-core backward (delta, rows and cols kernels)
         work.backward_prepare(77 + ctx.rank)
-        bwd_ms = max_over_ranks(statistics.mean(_timed_steps(work.backward_step, args.steps, args.warmup, ctx,
-                                                             flush)), ctx)
-        bwd_tflops = work.backward_flops / (bwd_ms * 1e-3) / 1e12
-        extra["backward"] = {"kernels": "delta_kernel + rows_kernel + cols_kernel (CUDA cores, fp32 accumulation)",
-                             "ms": round(bwd_ms, 4), "tflops": round(bwd_tflops, 3),
-                             "flops": "algorithmic 10*B*H*N^2*D",
-                             "frac_of_bf16_peak": round(bwd_tflops / peaks["bf16_tflops"], 4)}
+        kinds = (("backward", "auto"), ("backward_cuda_cores", "simt")) if work.dtype != torch.float32 else \
+            (("backward", "simt"),)
+        for key, kind in kinds:
+            bwd_ms = max_over_ranks(statistics.mean(_timed_steps(lambda: work.backward_step(kind), args.steps,
+                                                                 args.warmup, ctx, flush)), ctx)
+            bwd_tflops = work.backward_flops / (bwd_ms * 1e-3) / 1e12
+            kernels = ("sla_bwd_pds_kernel (tcgen05: P, dS and the slot gradient) + 3 batched GEMMs "
+                       "(dQ, dK, dV; cuBLAS)" if kind == "auto" else
+                       "delta_kernel + rows_kernel + cols_kernel (CUDA cores, fp32 accumulation)")
+            extra[key] = {"kernels": kernels, "ms": round(bwd_ms, 4), "tflops": round(bwd_tflops, 3),
+                          "flops": "algorithmic 10*B*H*N^2*D",
+                          "frac_of_bf16_peak": round(bwd_tflops / peaks["bf16_tflops"], 4)}
     elif isinstance(work, DenseLookGridWorkload):
         gbs = work.bytes / (per_launch_ms * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -140,6 +140,34 @@ typedef struct sla_backward_args {
  * P is recomputed from the LSE, no N x N buffer is needed beyond grad_dense. */
 INTP_API intp_status sla_backward(const sla_backward_args* args, void* stream);
 
+/* Probability / score-gradient pass of the backward on the tensor cores: the
+ * direct replacement of `_structured_look_probability_score_grad`
+ * (layers/triton_structured_look_attention.py:172-292, launched at :350-368).
+ * Writes, for every (b, h, query, key < N),
+ *   probability[b,h,q,k] = exp(scale q.k + bias - lse)
+ *   score_grad[b,h,q,k]  = probability * (dO.v_k - rowsum(dO * O))
+ * in fwd.dtype, row-major (B, H, N, ld); columns N .. round_up(N, 8) - 1 of
+ * each row receive 0, columns from round_up(N, 8) on are left untouched.
+ * The caller finishes the backward with the reference's batched products
+ * (:371-376): dQ = scale score_grad K, dK = scale score_grad^T Q,
+ * dV = probability^T dO.  With SLOTS bias, grad_pose (B, N-1, H, n_slots)
+ * fp32 (may be NULL) receives the per-slot sums of score_grad of each query
+ * row, which is the reference's grad_pose through one-hot fields (:378-395).
+ * Takes bf16 / f16, head_dim 64, bias NONE or SLOTS, no dense bias; anything
+ * else returns INTP_ERR_UNSUPPORTED (sla_backward covers it).  Needs fwd.lse;
+ * ld >= N, ld % 8 == 0, both outputs 16-byte aligned (INTP_ERR_LAYOUT).
+ * Errors inside the kernel (a wait that ran out) land in fwd.status.        */
+typedef struct sla_probability_score_grad_args {
+  sla_forward_args fwd;
+  const void* grad_out; int64_t grad_out_stride[4];
+  void* probability;
+  void* score_grad;
+  int64_t ld;
+  float* grad_pose;
+} sla_probability_score_grad_args;
+
+INTP_API intp_status sla_probability_score_grad(const sla_probability_score_grad_args* args, void* stream);
+
 /* Bytes needed by the packed slot table and the tile flags for sequence N. */
 INTP_API intp_status sla_slot_table_bytes(int64_t seq, int64_t* packed_bytes, int64_t* flag_bytes);
 

@@ -33,6 +33,7 @@ SLA_KERNEL_AUTO, SLA_KERNEL_SIMT, SLA_KERNEL_TCGEN05 = 0, 1, 2
 EXPORTED_SYMBOLS = (
     "sla_forward",
     "sla_backward",
+    "sla_probability_score_grad",
     "sla_slot_table_bytes",
     "sla_pack_slot_table",
     "nl1_forward",
@@ -99,6 +100,18 @@ class SlaBackwardArgs(ctypes.Structure):
         ("grad_fields", _vp),
         ("grad_dense", _vp),
         ("delta", _vp),
+    ]
+
+
+class SlaProbabilityScoreGradArgs(ctypes.Structure):
+    """Mirror of ``sla_probability_score_grad_args`` (field order and types must match)."""
+
+    _fields_ = [
+        ("fwd", SlaForwardArgs),
+        ("grad_out", _vp), ("grad_out_stride", _Stride),
+        ("probability", _vp), ("score_grad", _vp),
+        ("ld", _i64),
+        ("grad_pose", _vp),
     ]
 
 
@@ -173,6 +186,8 @@ def load() -> ctypes.CDLL:
         lib.sla_forward.restype = _i32
         lib.sla_backward.argtypes = [ctypes.POINTER(SlaBackwardArgs), _vp]
         lib.sla_backward.restype = _i32
+        lib.sla_probability_score_grad.argtypes = [ctypes.POINTER(SlaProbabilityScoreGradArgs), _vp]
+        lib.sla_probability_score_grad.restype = _i32
         lib.nl1_backward.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]
         lib.nl1_backward.restype = _i32
         lib.sla_slot_table_bytes.argtypes = [_i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]

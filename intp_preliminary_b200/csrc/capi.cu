@@ -255,6 +255,25 @@ intp_status sla_backward(const sla_backward_args* a, void* stream) {
   return intp::launch_sla_backward(bp, static_cast<cudaStream_t>(stream));
 }
 
+intp_status sla_probability_score_grad(const sla_probability_score_grad_args* a, void* stream) {
+  if (!a) return INTP_ERR_ARGUMENT;
+  intp::SlaParams p;
+  bool empty = false;
+  const intp_status st = to_params(&a->fwd, &p, &empty);
+  if (st != INTP_OK || empty) return st;
+  if (!a->fwd.lse || !a->grad_out || !a->probability || !a->score_grad) return INTP_ERR_ARGUMENT;
+  if (a->grad_pose && a->fwd.bias_mode != SLA_BIAS_SLOTS) return INTP_ERR_ARGUMENT;
+  if (a->grad_out_stride[3] != 1) return INTP_ERR_LAYOUT;
+  if (a->ld < a->fwd.seq || a->ld % 8 || reinterpret_cast<uintptr_t>(a->probability) % 16 ||
+      reinterpret_cast<uintptr_t>(a->score_grad) % 16)
+    return INTP_ERR_LAYOUT;
+  DeviceFacts f;
+  if (!device_facts(&f)) return INTP_ERR_LAUNCH;
+  if (f.major != 10) return INTP_ERR_ARCH;
+  return intp::launch_sla_probability_score_grad(p, a->grad_out, a->grad_out_stride, a->probability, a->score_grad,
+                                                 a->ld, a->grad_pose, static_cast<cudaStream_t>(stream));
+}
+
 intp_status nl1_forward(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
                         void* stream) {
   if (rows < 0 || protos < 0 || features < 0) return INTP_ERR_SHAPE;

@@ -64,6 +64,11 @@ int32_t sla_long_supported(const SlaParams& p);
 // prefers it when it applies.
 int32_t sla_short_supported(const SlaParams& p);
 int32_t launch_sla_short(const SlaParams& p, cudaStream_t stream, int sm_count);
+// Tensor-core probability / score-gradient pass (backward_tc.cu); returns
+// INTP_ERR_UNSUPPORTED (8) when the inputs do not qualify.
+int32_t launch_sla_probability_score_grad(const SlaParams& p, const void* dout, const int64_t* dout_stride,
+                                          void* probability, void* score_grad, int64_t ld, float* grad_pose,
+                                          cudaStream_t stream);
 int32_t launch_nl1(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
                    cudaStream_t stream);
 

@@ -305,14 +305,62 @@ def look_attention_forward(
     return out, lse
 
 
+def _backward_tensor_cores(q, k, v, out, lse, grad_out, pose, slots, scale, needs):
+    """SLOTS backward in the reference's two stages (layers/triton_structured_look_attention.py:341-376):
+    ``sla_probability_score_grad`` writes P and dS (16-bit, tensor cores) and
+    the per-slot pose gradient, then three batched GEMMs give dq, dk, dv.
+    Returns None when the tensor-core pass does not take the inputs."""
+    batch, heads, sequence, head_dim = q.shape
+    device = q.device
+    ld = (sequence + 7) // 8 * 8
+    probability = torch.empty(batch, heads, sequence, ld, dtype=q.dtype, device=device)
+    score_grad = torch.empty_like(probability)
+    dpose = (torch.empty(batch, sequence - 1, heads, pose.shape[-1], dtype=torch.float32, device=device)
+             if needs[3] else None)
+    fwd, keep = _forward_args(q, k, v, pose, slots, scale, None, out, lse, "auto")
+    args = _lib.SlaProbabilityScoreGradArgs()
+    args.fwd = fwd
+    args.grad_out, args.grad_out_stride = grad_out.data_ptr(), _stride4(grad_out)
+    args.probability, args.score_grad, args.ld = probability.data_ptr(), score_grad.data_ptr(), ld
+    args.grad_pose = dpose.data_ptr() if dpose is not None else None
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        status = lib.sla_probability_score_grad(ctypes.byref(args), ctypes.c_void_p(stream))
+    del keep
+    if status == _lib.INTP_ERR_UNSUPPORTED:
+        return None
+    _lib.check(status, "structured Look attention probability / score gradient")
+    bh = batch * heads
+    p = probability.view(bh, sequence, ld)[:, :, :sequence]
+    ds = score_grad.view(bh, sequence, ld)[:, :, :sequence]
+    shape = (bh, sequence, head_dim)
+    dq = dk = dv = None
+    if needs[0]:
+        dq = torch.baddbmm(q.new_empty(shape), ds, k.reshape(shape), beta=0, alpha=scale).view(q.shape)
+    if needs[1]:
+        dk = torch.baddbmm(k.new_empty(shape), ds.transpose(1, 2), q.reshape(shape), beta=0,
+                           alpha=scale).view(k.shape)
+    if needs[2]:
+        dv = torch.bmm(p.transpose(1, 2), grad_out.reshape(shape)).view(v.shape).to(v.dtype)
+    return dq, dk, dv, dpose.to(pose.dtype) if dpose is not None else None, None, None
+
+
 def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale, dense_bias=None,
-                            needs=(True, True, True, True, True, True)):
+                            needs=(True, True, True, True, True, True), kernel: str = "auto"):
     """Gradients of ``look_attention_forward`` (flash-style, from the forward's
     ``out`` and ``lse``).  Returns ``(dq, dk, dv, dpose, dfields, ddense)`` in the
     inputs' dtypes; entries whose ``needs`` flag is False, ``dfields`` for
     ``LookSlots`` fields (a table, not a tensor) and ``ddense`` without a dense
-    bias are None."""
+    bias are None.
+
+    ``kernel``: ``"auto"`` takes the tensor-core pass (bf16 / f16, head_dim 64,
+    slot tables, no dense bias) when it applies and the CUDA-core backward
+    otherwise; ``"simt"`` forces the CUDA-core backward; ``"tcgen05"`` raises
+    when the tensor-core pass cannot take the inputs."""
     _validate(q, k, v, pose, fields, dense_bias)
+    if kernel not in _KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
     device = q.device
     if grad_out.shape != q.shape or grad_out.device != device:
         raise ValueError("grad_output must match q in shape and device")
@@ -324,16 +372,23 @@ def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale,
         want = needs[3] or needs[4]
         dq, dk, dv, dslot, _, ddense = look_attention_backward(
             q, k, v, out, lse, grad_out, per_slot, fields.slots, scale=scale, dense_bias=dense_bias,
-            needs=(needs[0], needs[1], needs[2], want, False, needs[5]))
+            needs=(needs[0], needs[1], needs[2], want, False, needs[5]), kernel=kernel)
         dpose = torch.einsum("bqhs,hps->bqhp", dslot, sf).to(pose.dtype) if needs[3] else None
         dvalues = torch.einsum("bqhp,bqhs->hps", pose.float(), dslot).to(fields.values.dtype) if needs[4] else None
         return dq, dk, dv, dpose, dvalues, ddense
     grad_out = grad_out.to(q.dtype)
     if grad_out.stride(-1) != 1:
         grad_out = grad_out.contiguous()
+    slots = isinstance(fields, LookSlots)
+    if kernel != "simt" and slots and dense_bias is None and lse is not None:
+        grads = _backward_tensor_cores(q, k, v, out, lse, grad_out, pose, fields, scale, needs)
+        if grads is not None:
+            return grads
+    if kernel == "tcgen05":
+        raise ValueError("the tensor-core backward takes bf16 / f16 inputs with head_dim 64, "
+                         "a slot table and no dense bias")
     batch, heads, sequence, head_dim = q.shape
     patches = sequence - 1
-    slots = isinstance(fields, LookSlots)
     f32 = dict(dtype=torch.float32, device=device)
     dq = torch.empty(q.shape, **f32) if needs[0] else None
     dk = torch.empty(q.shape, **f32) if needs[1] else None

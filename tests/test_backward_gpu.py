@@ -88,7 +88,7 @@ def test_slot_gradients_match_reference_config1(cuda_device):
 
 
 def test_bf16_slot_backward_after_tensor_core_forward(cuda_device):
-    """bf16 forward on the tensor-core kernel (LSE from it), backward on CUDA cores,
+    """bf16 forward on the tensor-core kernel (LSE from it), backward (the tensor-core pass),
     against float64 autograd through the oracle."""
     rows = cols = 12
     n_dir, n_rad = 8, 4
@@ -179,3 +179,117 @@ def test_gradients_across_head_dims(cuda_device, head_dim):
     torch.testing.assert_close(out.detach().cpu().double(), ref.detach(), atol=3e-5, rtol=3e-5)
     for leaf, ref_leaf in zip(leaves, ref_leaves):
         torch.testing.assert_close(leaf.grad.cpu().double(), ref_leaf.grad, atol=3e-5, rtol=3e-5)
+
+
+def _slot_case(rows, cols, n_dir, n_rad, batch, heads, dtype, seed):
+    slots = LookSlots(hexgrid.synthetic_look_slots(rows, cols, n_dir, n_rad), n_dir * n_rad)
+    n = rows * cols + 1
+    gen = torch.Generator().manual_seed(seed)
+    q, k, v = ((torch.randn(batch, heads, n, 64, generator=gen) / 8).to(dtype) for _ in range(3))
+    pose = torch.rand(batch, n - 1, heads, n_dir * n_rad, generator=gen) * 2 - 1
+    grad_out = torch.randn(batch, heads, n, 64, generator=gen).to(dtype)
+    return slots, q, k, v, pose, grad_out
+
+
+def _onehot_fields(slots, heads):
+    n_slots = slots.n_slots
+    table = torch.from_numpy(slots.table.astype(np.int64))
+    onehot = torch.stack([(table == s).double() for s in range(n_slots)])
+    return onehot.unsqueeze(0).expand(heads, -1, -1, -1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("grid", [(14, 14, 12, 6), (20, 20, 8, 4), (3, 5, 4, 2)])
+def test_tensor_core_backward_matches_oracle(cuda_device, dtype, grid):
+    """The tensor-core backward (probability / score-gradient pass on tcgen05,
+    then batched GEMMs) against float64 autograd through the oracle: the model's
+    197 tokens with 72 slots, 401 tokens (4 query tiles, 7 key tiles, ragged
+    ends) and a 16-token case.  Bar: 2 % of the largest gradient, the bf16 bar
+    of the CUDA-core backward test above."""
+    rows, cols, n_dir, n_rad = grid
+    slots, q, k, v, pose, grad_out = _slot_case(rows, cols, n_dir, n_rad, 2, 3, dtype, seed=rows * 7 + n_dir)
+    dev = [t.to(cuda_device) for t in (q, k, v, pose)]
+    out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
+    grads = look_attention_backward(*dev[:3], out, lse, grad_out.to(cuda_device), dev[3], slots, scale=0.125,
+                                    kernel="tcgen05")
+    ref_leaves = [t.double().requires_grad_(True) for t in (q, k, v, pose)]
+    ref = reference_structured_look_attention(*ref_leaves, _onehot_fields(slots, 3), scale=0.125)
+    ref.backward(grad_out.double())
+    for got, ref_leaf in zip(grads[:4], ref_leaves):
+        assert got.dtype == ref_leaf.dtype or got.dtype in (dtype, torch.float32)
+        err = (got.cpu().double() - ref_leaf.grad).abs().max().item()
+        assert err <= 2e-2 * max(ref_leaf.grad.abs().max().item(), 1e-3), err
+
+
+def test_tensor_core_backward_agrees_with_cuda_core_backward(cuda_device):
+    """Both backward implementations on the same bf16 inputs at the model's
+    shape (batch 4): within the 16-bit rounding of P and dS."""
+    slots, q, k, v, pose, grad_out = _slot_case(14, 14, 12, 6, 4, 3, torch.bfloat16, seed=5)
+    dev = [t.to(cuda_device) for t in (q, k, v, pose)]
+    out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
+    go = grad_out.to(cuda_device)
+    tc = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05")
+    simt = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="simt")
+    for a, b in zip(tc[:4], simt[:4]):
+        err = (a.float() - b.float()).abs().max().item()
+        assert err <= 1e-2 * max(b.float().abs().max().item(), 1e-3), err
+
+
+def test_probability_and_score_grad_tensors(cuda_device):
+    """The pass's own outputs, P and dS (the reference's `probability` and
+    `score_grad`, layers/triton_structured_look_attention.py:283-292), against
+    float64 values computed from the same bf16 inputs; zeros up to the next
+    multiple of 8 columns past N and the padding beyond it untouched."""
+    import ctypes
+
+    from intp_preliminary_b200 import _lib
+    from intp_preliminary_b200.look_attention import _forward_args, _stride4
+
+    slots, q, k, v, pose, grad_out = _slot_case(9, 11, 6, 3, 2, 2, torch.bfloat16, seed=9)
+    n = q.shape[2]
+    dev = [t.to(cuda_device) for t in (q, k, v, pose)]
+    out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
+    go = grad_out.to(cuda_device)
+    ld = (n + 7) // 8 * 8 + 8
+    prob = torch.full((2, 2, n, ld), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    sgrad = torch.full_like(prob, 7.0)
+    fwd, keep = _forward_args(*dev, slots, 0.125, None, out, lse, "auto")
+    args = _lib.SlaProbabilityScoreGradArgs()
+    args.fwd = fwd
+    args.grad_out, args.grad_out_stride = go.data_ptr(), _stride4(go)
+    args.probability, args.score_grad, args.ld = prob.data_ptr(), sgrad.data_ptr(), ld
+    args.grad_pose = None
+    status = _lib.load().sla_probability_score_grad(ctypes.byref(args),
+                                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert status == 0
+    torch.cuda.synchronize()
+    bias = torch.zeros(2, 2, n, n, dtype=torch.float64)
+    onehot = _onehot_fields(slots, 2)
+    bias[:, :, 1:, 1:] = torch.einsum("bqhp,hpqk->bhqk", pose.double(), onehot)
+    s = torch.einsum("bhqd,bhkd->bhqk", q.double(), k.double()) * 0.125 + bias
+    p_ref = torch.softmax(s, dim=-1)
+    o = out.cpu().double()
+    dp = torch.einsum("bhqd,bhkd->bhqk", grad_out.double(), v.double())
+    delta = (grad_out.double() * o).sum(-1, keepdim=True)
+    ds_ref = p_ref * (dp - delta)
+    got_p = prob.cpu().double()
+    got_ds = sgrad.cpu().double()
+    assert (got_p[..., :n] - p_ref).abs().max().item() <= 4e-3 * p_ref.abs().max().item() + 1e-4
+    assert (got_ds[..., :n] - ds_ref).abs().max().item() <= 1e-2 * ds_ref.abs().max().item() + 1e-4
+    n8 = (n + 7) // 8 * 8  # the last 16-byte chunk of a row is written whole, with zeros past N
+    assert (got_p[..., n:n8] == 0).all() and (got_ds[..., n:n8] == 0).all()
+    assert (got_p[..., n8:] == 7.0).all() and (got_ds[..., n8:] == 7.0).all()
+    del keep
+
+
+def test_tensor_core_backward_declines_other_inputs(cuda_device):
+    """fp32 inputs (or dense fields) are outside the tensor-core pass: "auto"
+    takes the CUDA-core backward, "tcgen05" raises."""
+    slots, q, k, v, pose, grad_out = _slot_case(4, 4, 4, 2, 1, 2, torch.float32, seed=3)
+    dev = [t.to(cuda_device) for t in (q, k, v, pose)]
+    out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
+    go = grad_out.to(cuda_device)
+    grads = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125)
+    assert grads[0].dtype == torch.float32
+    with pytest.raises(ValueError):
+        look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05")
