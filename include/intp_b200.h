@@ -122,7 +122,10 @@ INTP_API intp_status sla_forward(const sla_forward_args* args, void* stream);
  *   grad_fields            : (H, P, Np, Np)  (FIELDS mode; zero-filled by the
  *                            caller, accumulated with atomics over the batch)
  *   grad_dense             : (B, H, Np, Np)  (when fwd.dense is set)
- * delta: (B, H, N) float32 scratch.                                          */
+ * delta: (B, H, N) float32 scratch (receives rowsum(dO * O)).
+ * slots_packed_t: SLOTS mode, the tensor-core path only: the slot table
+ * transposed (slots_t[k][q] = slots[q][k]) and packed by sla_pack_slot_table
+ * (same sizes as fwd.slots_packed); NULL keeps SLOTS on the CUDA-core path.  */
 typedef struct sla_backward_args {
   sla_forward_args fwd;
   const void* grad_out; int64_t grad_out_stride[4];
@@ -131,13 +134,22 @@ typedef struct sla_backward_args {
   float* grad_fields;
   float* grad_dense;
   float* delta;
+  const uint8_t* slots_packed_t;
 } sla_backward_args;
 
 /* Structured Look attention backward.  Replaces the launch of
  * `_structured_look_probability_score_grad` and the batched matmuls that follow
  * it in `_StructuredLookAttention.backward`
  * (layers/triton_structured_look_attention.py:172-292, 341-409); flash-style:
- * P is recomputed from the LSE, no N x N buffer is needed beyond grad_dense. */
+ * P is recomputed from the LSE, no N x N buffer is needed beyond grad_dense.
+ * fwd.kernel selects the implementation: SLA_KERNEL_AUTO takes the tensor
+ * cores (two tcgen05 kernels: dQ with delta and the slot gradient per query
+ * tile, then dK and dV per key tile; bf16 / f16, head_dim 64, no bias or SLOTS
+ * with slots_packed_t, no dense bias, no grad_fields) when the request
+ * qualifies and the CUDA cores otherwise; SLA_KERNEL_SIMT forces the CUDA
+ * cores; SLA_KERNEL_TCGEN05 returns INTP_ERR_UNSUPPORTED when the tensor-core
+ * path cannot take the request.  Deterministic on both paths except FIELDS
+ * grad_fields (atomics over the batch).                                      */
 INTP_API intp_status sla_backward(const sla_backward_args* args, void* stream);
 
 /* Probability / score-gradient pass of the backward on the tensor cores: the

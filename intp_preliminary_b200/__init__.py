@@ -9,7 +9,7 @@ The compute runs in ``_lib/libintp_b200.so`` (built by ``build.py``).
 """
 
 from .look_attention import (LookSlotFields, LookSlots, check_device_status, look_attention_backward,
-                             look_attention_forward, structured_look_attention)
+                             look_attention_forward, look_probability_score_grad, structured_look_attention)
 from .negative_l1 import negative_l1_backward, negative_l1_distance, negative_l1_forward
 from .dense_look_grid import (dense_look_grid_backward, dense_look_grid_forward, dense_look_grid_sample,
                               look_sampling_tables)
@@ -20,6 +20,7 @@ __all__ = [
     "check_device_status",
     "look_attention_backward",
     "look_attention_forward",
+    "look_probability_score_grad",
     "structured_look_attention",
     "negative_l1_distance",
     "negative_l1_backward",

@@ -26,7 +26,7 @@ INTP_ERR_UNSUPPORTED = 8
 INTP_F32, INTP_F16, INTP_BF16 = 0, 1, 2
 SLA_BIAS_NONE, SLA_BIAS_FIELDS, SLA_BIAS_SLOTS, SLA_BIAS_SLOT_FIELDS = 0, 1, 2, 3
 SLA_SLOT_NONE = 255
-ABI_VERSION = 2
+ABI_VERSION = 3
 SLA_KERNEL_AUTO, SLA_KERNEL_SIMT, SLA_KERNEL_TCGEN05 = 0, 1, 2
 
 # Every symbol include/intp_b200.h declares.
@@ -100,6 +100,7 @@ class SlaBackwardArgs(ctypes.Structure):
         ("grad_fields", _vp),
         ("grad_dense", _vp),
         ("delta", _vp),
+        ("slots_packed_t", _vp),
     ]
 
 

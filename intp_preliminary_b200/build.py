@@ -24,7 +24,7 @@ INCLUDE = PACKAGE_DIR.parent / "include"
 LIB_DIR = PACKAGE_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libintp_b200.so"
 SOURCES = ("capi.cu", "look_attention_simt.cu", "look_attention_tc.cu", "look_attention_short.cu", "negative_l1.cu",
-           "noalloc.cu", "share_vit_ops.cu", "backward.cu", "backward_tc.cu", "gemm_epilogue.cu", "dense_look_grid.cu")
+           "noalloc.cu", "share_vit_ops.cu", "backward.cu", "backward_tc.cu", "backward_fused.cu", "gemm_epilogue.cu", "dense_look_grid.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

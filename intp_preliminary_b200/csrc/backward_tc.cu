@@ -14,12 +14,15 @@
 // and writes P and dS in the input dtype (the reference's `probability` and
 // `score_grad`); the caller applies the softmax scale in the dQ / dK GEMMs.
 //
-// CTA: 160 threads, one (batch, head, 128-query tile) per CTA: warps 0-3 own
-// one query row per thread (TMEM lane); warp 4 lane 0 issues the TMA loads
-// (Q, dO once; K / V tiles through a 2-stage ring) and the MMAs (S and dP into
-// one of two TMEM buffers).  Each row thread reads its 64 slot bytes of a tile
-// straight from the packed pair table (L2) while it waits for the tile's
-// scores.  Every mbarrier wait is bounded.
+// CTA: 288 threads, one (batch, head, 128-query tile) per CTA.  Warps 0-7 are
+// two warpgroups of row threads: thread t owns query row t % 128 (its TMEM
+// lane) and keys 0-31 (t < 128) or 32-63 of every key tile.  Warp 8 lane 0
+// issues the TMA loads (Q, dO once; K / V tiles through a 2-stage ring) and the
+// MMAs (S and dP into one of two TMEM buffers).  Each row thread reads its 32
+// slot bytes of a tile straight from the packed pair table (L2) while it waits
+// for the tile's scores; each warpgroup keeps its per-slot gradient sums in
+// its own shared [slot][row] array (one writer per cell), added at the end.
+// Every mbarrier wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,7 +39,9 @@ namespace {
 constexpr int BQ = 128;                     // query rows per tile
 constexpr int BK = 64;                      // keys per tile
 constexpr int D64 = 64;
-constexpr int kBwdThreads = 160;
+constexpr int kRowThreads = 256;          // two warpgroups: keys 0-31 / 32-63 of each tile
+constexpr int kBwdThreads = kRowThreads + 32;
+constexpr int kMmaWarp = kRowThreads / 32;
 constexpr uint32_t kTile128 = BQ * D64 * 2;  // 16 KB
 constexpr uint32_t kTile64 = BK * D64 * 2;   // 8 KB
 
@@ -67,6 +72,9 @@ template <bool BF16>
 __device__ __forceinline__ uint32_t pk2(float lo, float hi) {
   return BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
+
+// Barrier of the row threads only (named barrier 1).
+__device__ __forceinline__ void row_threads_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kRowThreads) : "memory"); }
 
 template <bool BF16>
 __device__ __forceinline__ float ld16(const void* p, int64_t idx) {
@@ -106,13 +114,13 @@ sla_bwd_pds_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], 4);
+      mbar_init(&bars->s_free[s], kRowThreads / 32);
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     mbar_fence_init();
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&bars->tmem_base, 256);
     tmem_relinquish();
   }
@@ -121,7 +129,7 @@ sla_bwd_pds_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     // ------------------------------------------------------------ loads + MMAs (one thread)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -202,10 +210,11 @@ sla_bwd_pds_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     }
   } else {
     // ------------------------------------------------------------ row threads
-    const int row = threadIdx.x;                    // 0..127 = TMEM lane
+    const int row = threadIdx.x & (BQ - 1);         // 0..127 = TMEM lane
+    const int half = threadIdx.x >> 7;              // this thread's 32 keys of each tile
     const int32_t i = qt * BQ + row;                // query token
     const bool valid = i < N;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 32 * half;
     const float scale_log2 = p.scale * kLog2eF;
     // delta = rowsum(dO * O) and the row's LSE (log2 domain)
     float delta = 0.f, lse2 = 0.f;
@@ -217,10 +226,12 @@ sla_bwd_pds_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       lse2 = p.lse[(int64_t(b) * H + h) * N + i] * kLog2eF;
     }
     float* trow = table_s + row;
-    float* drow = dacc_s + row;
+    // one slot-sum array per warpgroup: each cell has one writer (this thread)
+    float* drow = dacc_s + half * (a.n_slots + 2) * BQ + row;
     if (use_bias) {
-      stage_table(table_s, a, b, h, i, row);  // log2-domain Look values; [ns] = 0, [ns+1] = -inf
+      if (half == 0) stage_table(table_s, a, b, h, i, row);  // log2-domain Look values; [ns] = 0, [ns+1] = -inf
       for (int s = 0; s < a.n_slots + 2; ++s) drow[s * BQ] = 0.f;
+      row_threads_sync();
     }
     const uint8_t* sbase = p.slots_packed + int64_t(qt) * n_kt * kSlotTileBytes + row * 16;
     const int64_t orow = (int64_t(bh) * N + i) * a.ld;  // element offset of this row in P / dS
@@ -228,57 +239,67 @@ sla_bwd_pds_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     for (int j = 0; j < n_kt && ok; ++j) {
       const int st = j & 1;
       // this row's 64 slot bytes of the tile (L2), in flight during the wait
-      uint4 cur[4];
+      uint4 cur[2];
       if (use_bias) {
-        const uint8_t* src = sbase + int64_t(j) * kSlotTileBytes;
+        const uint8_t* src = sbase + int64_t(j) * kSlotTileBytes + half * 4096;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) cur[c] = __ldg(reinterpret_cast<const uint4*>(src + c * 2048));
+        for (int c = 0; c < 2; ++c) cur[c] = __ldg(reinterpret_cast<const uint4*>(src + c * 2048));
       }
       if (!mbar_wait(&bars->s_full[st], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sr[64], dr[64];
+      uint32_t sr[32], dr[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         tmem_ld16(lane_base + st * 128 + c * 16, *reinterpret_cast<uint32_t(*)[16]>(sr + 16 * c));
         tmem_ld16(lane_base + st * 128 + 64 + c * 16, *reinterpret_cast<uint32_t(*)[16]>(dr + 16 * c));
       }
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         reg_fence16(*reinterpret_cast<uint32_t(*)[16]>(sr + 16 * c));
         reg_fence16(*reinterpret_cast<uint32_t(*)[16]>(dr + 16 * c));
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_free[st]);  // the MMA may overwrite buffer st
-      const int32_t k0 = j * BK;
+      const int32_t k0 = j * BK + 32 * half;
       uint8_t* pdst = static_cast<uint8_t*>(a.p_out) + 2 * (orow + k0);
       uint8_t* ddst = static_cast<uint8_t*>(a.ds_out) + 2 * (orow + k0);
 #pragma unroll
-      for (int c = 0; c < BK / 8; ++c) {  // 8 keys: one 16-byte store of P and of dS
+      for (int c = 0; c < 4; ++c) {  // 8 keys: one 16-byte store of P and of dS
         uint32_t pw[4], dw[4];
+        if (use_bias) {
+          // all eight table reads first, then the math, then the eight slot-sum updates
+          uint32_t sl[8];
+          float tb[8], g[8];
 #pragma unroll
-        for (int e2 = 0; e2 < 8; e2 += 2) {
-          const int e = 8 * c + e2;
-          float t0, t1;
-          if (use_bias) {
-            const uint32_t word = (&cur[e >> 4].x)[(e & 15) >> 2];
-            const uint32_t s0 = __byte_perm(word, 0u, 0x4440u | (e & 3));
-            const uint32_t s1 = __byte_perm(word, 0u, 0x4440u | ((e + 1) & 3));
-            t0 = fmaf(__uint_as_float(sr[e]), scale_log2, trow[s0 * BQ]);
-            t1 = fmaf(__uint_as_float(sr[e + 1]), scale_log2, trow[s1 * BQ]);
-            const float p0 = fast_exp2(t0 - lse2), p1 = fast_exp2(t1 - lse2);
-            const float g0 = p0 * (__uint_as_float(dr[e]) - delta), g1 = p1 * (__uint_as_float(dr[e + 1]) - delta);
-            drow[s0 * BQ] += g0;  // slot gradient ([ns], [ns + 1]: sinks)
-            drow[s1 * BQ] += g1;
+          for (int e2 = 0; e2 < 8; ++e2) {
+            const int e = 8 * c + e2;
+            sl[e2] = __byte_perm((&cur[e >> 4].x)[(e & 15) >> 2], 0u, 0x4440u | (e & 3));
+            tb[e2] = trow[sl[e2] * BQ];
+          }
+#pragma unroll
+          for (int e2 = 0; e2 < 8; e2 += 2) {
+            const int e = 8 * c + e2;
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[e]), scale_log2, tb[e2]) - lse2);
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[e + 1]), scale_log2, tb[e2 + 1]) - lse2);
+            g[e2] = p0 * (__uint_as_float(dr[e]) - delta);
+            g[e2 + 1] = p1 * (__uint_as_float(dr[e + 1]) - delta);
             pw[e2 / 2] = pk2<BF16>(p0, p1);
-            dw[e2 / 2] = pk2<BF16>(g0, g1);
-          } else {
-            t0 = k0 + e < N ? __uint_as_float(sr[e]) * scale_log2 : -INFINITY;
-            t1 = k0 + e + 1 < N ? __uint_as_float(sr[e + 1]) * scale_log2 : -INFINITY;
+            dw[e2 / 2] = pk2<BF16>(g[e2], g[e2 + 1]);
+          }
+#pragma unroll
+#pragma unroll
+          for (int e2 = 0; e2 < 8; ++e2) drow[sl[e2] * BQ] += g[e2];  // [ns], [ns + 1]: sinks
+        } else {
+#pragma unroll
+          for (int e2 = 0; e2 < 8; e2 += 2) {
+            const int e = 8 * c + e2;
+            const float t0 = k0 + e < N ? __uint_as_float(sr[e]) * scale_log2 : -INFINITY;
+            const float t1 = k0 + e + 1 < N ? __uint_as_float(sr[e + 1]) * scale_log2 : -INFINITY;
             const float p0 = fast_exp2(t0 - lse2), p1 = fast_exp2(t1 - lse2);
             const float g0 = p0 * (__uint_as_float(dr[e]) - delta), g1 = p1 * (__uint_as_float(dr[e + 1]) - delta);
             pw[e2 / 2] = pk2<BF16>(p0, p1);
@@ -291,16 +312,18 @@ sla_bwd_pds_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         }
       }
     }
-    if (ok && use_bias && a.grad_pose != nullptr && valid && i >= 1) {
+    if (use_bias) row_threads_sync();  // both warpgroups' slot sums are in
+    if (ok && use_bias && half == 0 && a.grad_pose != nullptr && valid && i >= 1) {
       const int64_t np = N - 1;
       float* dst = a.grad_pose + ((int64_t(b) * np + (i - 1)) * H + h) * a.n_slots;
-      for (int s = 0; s < a.n_slots; ++s) dst[s] = drow[s * BQ];
+      const float* other = drow + (a.n_slots + 2) * BQ;
+      for (int s = 0; s < a.n_slots; ++s) dst[s] = drow[s * BQ] + other[s * BQ];
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
@@ -345,7 +368,7 @@ int32_t launch_sla_probability_score_grad(const SlaParams& p, const void* dout, 
   a.off_table = off;
   off += table_bytes;
   a.off_dacc = off;
-  off += table_bytes;
+  off += 2 * table_bytes;
   a.off_bars = align16(off, 64);
   const size_t smem = a.off_bars + sizeof(BwdBars) + 1024;
   const int64_t grid = p.batch * p.heads * a.n_qt;

@@ -53,7 +53,7 @@ uint64_t tc_wait_budget_ns() { return g_wait_budget_ns.load(std::memory_order_re
 
 extern "C" {
 
-int32_t intp_abi_version(void) { return 2; }
+int32_t intp_abi_version(void) { return 3; }
 
 const char* intp_status_string(intp_status s) {
   switch (s) {
@@ -252,7 +252,11 @@ intp_status sla_backward(const sla_backward_args* a, void* stream) {
   bp.grad_fields = a->grad_fields;
   bp.grad_dense = a->grad_dense;
   bp.delta = a->delta;
-  return intp::launch_sla_backward(bp, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->fwd.kernel != SLA_KERNEL_SIMT && intp::sla_backward_fused_supported(bp, a->slots_packed_t))
+    return intp::launch_sla_backward_fused(bp, a->slots_packed_t, s);
+  if (a->fwd.kernel == SLA_KERNEL_TCGEN05) return INTP_ERR_UNSUPPORTED;
+  return intp::launch_sla_backward(bp, s);
 }
 
 intp_status sla_probability_score_grad(const sla_probability_score_grad_args* a, void* stream) {

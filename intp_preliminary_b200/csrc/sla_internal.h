@@ -69,6 +69,10 @@ int32_t launch_sla_short(const SlaParams& p, cudaStream_t stream, int sm_count);
 int32_t launch_sla_probability_score_grad(const SlaParams& p, const void* dout, const int64_t* dout_stride,
                                           void* probability, void* score_grad, int64_t ld, float* grad_pose,
                                           cudaStream_t stream);
+// Fused tensor-core backward (backward_fused.cu): dQ / delta / slot gradient,
+// then dK / dV.  `slots_t` is the transposed packed slot table (SLOTS mode).
+int32_t sla_backward_fused_supported(const SlaBwdParams& bp, const uint8_t* slots_t);
+int32_t launch_sla_backward_fused(const SlaBwdParams& bp, const uint8_t* slots_t, cudaStream_t stream);
 int32_t launch_nl1(const float* x, const float* w, float* out, int64_t rows, int64_t protos, int64_t features,
                    cudaStream_t stream);
 

@@ -67,6 +67,8 @@ class LookSlots:
         self.heads = heads
         self._packed: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self._host: tuple[np.ndarray, np.ndarray] | None = None
+        self._packed_t: dict[int, torch.Tensor] = {}
+        self._host_t: np.ndarray | None = None
         self._lock = threading.Lock()
 
     @property
@@ -95,6 +97,29 @@ class LookSlots:
             )
             self._host = (packed, flags)
         return self._host
+
+    def host_packed_t(self) -> np.ndarray:
+        """Packed tiles of the transposed table (``[k, q]``), read by the key-major
+        backward kernel (pure CPU)."""
+        if self._host_t is None:
+            lib = _lib.load()
+            packed, flags = (np.empty_like(x) for x in self.host_packed())
+            table_t = np.ascontiguousarray(self.table.T)
+            _lib.check(
+                lib.sla_pack_slot_table(
+                    table_t.ctypes.data, self.patch_count, self.n_slots, packed.ctypes.data, flags.ctypes.data
+                ),
+                "sla_pack_slot_table",
+            )
+            self._host_t = packed
+        return self._host_t
+
+    def device_packed_t(self, device: torch.device) -> torch.Tensor:
+        index = torch.device(device).index
+        with self._lock:
+            if index not in self._packed_t:
+                self._packed_t[index] = torch.from_numpy(self.host_packed_t()).to(device)
+            return self._packed_t[index]
 
     def device_packed(self, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
         index = torch.device(device).index
@@ -305,45 +330,42 @@ def look_attention_forward(
     return out, lse
 
 
-def _backward_tensor_cores(q, k, v, out, lse, grad_out, pose, slots, scale, needs):
-    """SLOTS backward in the reference's two stages (layers/triton_structured_look_attention.py:341-376):
-    ``sla_probability_score_grad`` writes P and dS (16-bit, tensor cores) and
-    the per-slot pose gradient, then three batched GEMMs give dq, dk, dv.
-    Returns None when the tensor-core pass does not take the inputs."""
+def look_probability_score_grad(q, k, v, out, lse, grad_out, pose, slots: "LookSlots", *, scale):
+    """The reference's probability / score-gradient pass
+    (``_structured_look_probability_score_grad``,
+    layers/triton_structured_look_attention.py:172-292) on the tensor cores:
+    returns ``(probability, score_grad, grad_pose)`` with the first two
+    ``(B, H, N, N)`` in q's dtype (views of row-padded buffers) and
+    ``grad_pose`` ``(B, N-1, H, n_slots)`` float32, the per-slot sums of
+    ``score_grad`` (the reference's pose gradient through one-hot fields).
+    bf16 / f16, head_dim 64; anything else raises ValueError."""
+    _validate(q, k, v, pose, slots, None)
+    if not isinstance(slots, LookSlots):
+        raise ValueError("look_probability_score_grad takes a LookSlots table")
     batch, heads, sequence, head_dim = q.shape
     device = q.device
+    grad_out = grad_out.to(q.dtype)
+    if grad_out.stride(-1) != 1:
+        grad_out = grad_out.contiguous()
     ld = (sequence + 7) // 8 * 8
     probability = torch.empty(batch, heads, sequence, ld, dtype=q.dtype, device=device)
     score_grad = torch.empty_like(probability)
-    dpose = (torch.empty(batch, sequence - 1, heads, pose.shape[-1], dtype=torch.float32, device=device)
-             if needs[3] else None)
+    dpose = torch.empty(batch, sequence - 1, heads, pose.shape[-1], dtype=torch.float32, device=device)
     fwd, keep = _forward_args(q, k, v, pose, slots, scale, None, out, lse, "auto")
     args = _lib.SlaProbabilityScoreGradArgs()
     args.fwd = fwd
     args.grad_out, args.grad_out_stride = grad_out.data_ptr(), _stride4(grad_out)
     args.probability, args.score_grad, args.ld = probability.data_ptr(), score_grad.data_ptr(), ld
-    args.grad_pose = dpose.data_ptr() if dpose is not None else None
+    args.grad_pose = dpose.data_ptr()
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
         status = lib.sla_probability_score_grad(ctypes.byref(args), ctypes.c_void_p(stream))
     del keep
     if status == _lib.INTP_ERR_UNSUPPORTED:
-        return None
+        raise ValueError("the probability / score-gradient pass takes bf16 / f16 inputs with head_dim 64")
     _lib.check(status, "structured Look attention probability / score gradient")
-    bh = batch * heads
-    p = probability.view(bh, sequence, ld)[:, :, :sequence]
-    ds = score_grad.view(bh, sequence, ld)[:, :, :sequence]
-    shape = (bh, sequence, head_dim)
-    dq = dk = dv = None
-    if needs[0]:
-        dq = torch.baddbmm(q.new_empty(shape), ds, k.reshape(shape), beta=0, alpha=scale).view(q.shape)
-    if needs[1]:
-        dk = torch.baddbmm(k.new_empty(shape), ds.transpose(1, 2), q.reshape(shape), beta=0,
-                           alpha=scale).view(k.shape)
-    if needs[2]:
-        dv = torch.bmm(p.transpose(1, 2), grad_out.reshape(shape)).view(v.shape).to(v.dtype)
-    return dq, dk, dv, dpose.to(pose.dtype) if dpose is not None else None, None, None
+    return probability[..., :sequence], score_grad[..., :sequence], dpose
 
 
 def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale, dense_bias=None,
@@ -354,10 +376,10 @@ def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale,
     ``LookSlots`` fields (a table, not a tensor) and ``ddense`` without a dense
     bias are None.
 
-    ``kernel``: ``"auto"`` takes the tensor-core pass (bf16 / f16, head_dim 64,
-    slot tables, no dense bias) when it applies and the CUDA-core backward
-    otherwise; ``"simt"`` forces the CUDA-core backward; ``"tcgen05"`` raises
-    when the tensor-core pass cannot take the inputs."""
+    ``kernel``: ``"auto"`` takes the tensor-core backward (bf16 / f16,
+    head_dim 64, slot tables, no dense bias) when it applies and the CUDA-core
+    backward otherwise; ``"simt"`` forces the CUDA-core backward; ``"tcgen05"``
+    raises when the tensor-core backward cannot take the inputs."""
     _validate(q, k, v, pose, fields, dense_bias)
     if kernel not in _KERNELS:
         raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
@@ -380,13 +402,6 @@ def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale,
     if grad_out.stride(-1) != 1:
         grad_out = grad_out.contiguous()
     slots = isinstance(fields, LookSlots)
-    if kernel != "simt" and slots and dense_bias is None and lse is not None:
-        grads = _backward_tensor_cores(q, k, v, out, lse, grad_out, pose, fields, scale, needs)
-        if grads is not None:
-            return grads
-    if kernel == "tcgen05":
-        raise ValueError("the tensor-core backward takes bf16 / f16 inputs with head_dim 64, "
-                         "a slot table and no dense bias")
     batch, heads, sequence, head_dim = q.shape
     patches = sequence - 1
     f32 = dict(dtype=torch.float32, device=device)
@@ -397,9 +412,14 @@ def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale,
     dfields = torch.zeros(fields.shape, **f32) if needs[4] and not slots else None
     ddense = torch.empty(batch, heads, patches, patches, **f32) if needs[5] and dense_bias is not None else None
     delta = torch.empty(batch, heads, sequence, **f32)
-    fwd, keep = _forward_args(q, k, v, pose, fields, scale, dense_bias, out, lse, "simt")
+    pose_k = pose
+    if slots and kernel != "simt" and (pose.dtype != torch.float32 or pose.stride(-1) != 1):
+        pose_k = pose.float().contiguous()  # the tensor-core path copies fp32 pose rows
+    fwd, keep = _forward_args(q, k, v, pose_k, fields, scale, dense_bias, out, lse, kernel)
     args = _lib.SlaBackwardArgs()
     args.fwd = fwd
+    if slots and kernel != "simt":
+        args.slots_packed_t = fields.device_packed_t(device).data_ptr()
     args.grad_out, args.grad_out_stride = grad_out.data_ptr(), _stride4(grad_out)
     for name, t in (("grad_q", dq), ("grad_k", dk), ("grad_v", dv), ("grad_pose", dpose), ("grad_fields", dfields),
                     ("grad_dense", ddense), ("delta", delta)):
@@ -408,6 +428,9 @@ def look_attention_backward(q, k, v, out, lse, grad_out, pose, fields, *, scale,
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
         status = lib.sla_backward(ctypes.byref(args), ctypes.c_void_p(stream))
+    if status == _lib.INTP_ERR_UNSUPPORTED and kernel == "tcgen05":
+        raise ValueError("the tensor-core backward takes bf16 / f16 inputs with head_dim 64, "
+                         "a slot table and no dense bias")
     _lib.check(status, "structured Look attention backward")
     del keep
     return (dq.to(q.dtype) if dq is not None else None,

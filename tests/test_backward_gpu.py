@@ -236,33 +236,18 @@ def test_tensor_core_backward_agrees_with_cuda_core_backward(cuda_device):
 
 
 def test_probability_and_score_grad_tensors(cuda_device):
-    """The pass's own outputs, P and dS (the reference's `probability` and
-    `score_grad`, layers/triton_structured_look_attention.py:283-292), against
-    float64 values computed from the same bf16 inputs; zeros up to the next
-    multiple of 8 columns past N and the padding beyond it untouched."""
-    import ctypes
-
-    from intp_preliminary_b200 import _lib
-    from intp_preliminary_b200.look_attention import _forward_args, _stride4
+    """look_probability_score_grad (the reference's `probability` and
+    `score_grad`, layers/triton_structured_look_attention.py:283-292, and the
+    per-slot pose gradient) against float64 values from the same bf16 inputs."""
+    from intp_preliminary_b200 import look_probability_score_grad
 
     slots, q, k, v, pose, grad_out = _slot_case(9, 11, 6, 3, 2, 2, torch.bfloat16, seed=9)
     n = q.shape[2]
     dev = [t.to(cuda_device) for t in (q, k, v, pose)]
     out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
-    go = grad_out.to(cuda_device)
-    ld = (n + 7) // 8 * 8 + 8
-    prob = torch.full((2, 2, n, ld), 7.0, dtype=torch.bfloat16, device=cuda_device)
-    sgrad = torch.full_like(prob, 7.0)
-    fwd, keep = _forward_args(*dev, slots, 0.125, None, out, lse, "auto")
-    args = _lib.SlaProbabilityScoreGradArgs()
-    args.fwd = fwd
-    args.grad_out, args.grad_out_stride = go.data_ptr(), _stride4(go)
-    args.probability, args.score_grad, args.ld = prob.data_ptr(), sgrad.data_ptr(), ld
-    args.grad_pose = None
-    status = _lib.load().sla_probability_score_grad(ctypes.byref(args),
-                                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert status == 0
-    torch.cuda.synchronize()
+    prob, sgrad, dpose = look_probability_score_grad(*dev[:3], out, lse, grad_out.to(cuda_device), dev[3], slots,
+                                                     scale=0.125)
+    assert prob.shape == (2, 2, n, n) and prob.dtype == torch.bfloat16
     bias = torch.zeros(2, 2, n, n, dtype=torch.float64)
     onehot = _onehot_fields(slots, 2)
     bias[:, :, 1:, 1:] = torch.einsum("bqhp,hpqk->bhqk", pose.double(), onehot)
@@ -272,14 +257,65 @@ def test_probability_and_score_grad_tensors(cuda_device):
     dp = torch.einsum("bhqd,bhkd->bhqk", grad_out.double(), v.double())
     delta = (grad_out.double() * o).sum(-1, keepdim=True)
     ds_ref = p_ref * (dp - delta)
-    got_p = prob.cpu().double()
-    got_ds = sgrad.cpu().double()
-    assert (got_p[..., :n] - p_ref).abs().max().item() <= 4e-3 * p_ref.abs().max().item() + 1e-4
-    assert (got_ds[..., :n] - ds_ref).abs().max().item() <= 1e-2 * ds_ref.abs().max().item() + 1e-4
-    n8 = (n + 7) // 8 * 8  # the last 16-byte chunk of a row is written whole, with zeros past N
-    assert (got_p[..., n:n8] == 0).all() and (got_ds[..., n:n8] == 0).all()
-    assert (got_p[..., n8:] == 7.0).all() and (got_ds[..., n8:] == 7.0).all()
-    del keep
+    assert (prob.cpu().double() - p_ref).abs().max().item() <= 4e-3 * p_ref.abs().max().item() + 1e-4
+    assert (sgrad.cpu().double() - ds_ref).abs().max().item() <= 1e-2 * ds_ref.abs().max().item() + 1e-4
+    dpose_ref = torch.einsum("bhqk,hpqk->bqhp", ds_ref[:, :, 1:, 1:], onehot)
+    assert (dpose.cpu().double() - dpose_ref).abs().max().item() <= 1e-2 * dpose_ref.abs().max().item() + 1e-5
+
+
+def test_fused_backward_is_deterministic(cuda_device):
+    """Every gradient element of the fused tensor-core backward has one writer
+    (no atomics): two runs agree bit for bit."""
+    slots, q, k, v, pose, grad_out = _slot_case(14, 14, 12, 6, 4, 3, torch.bfloat16, seed=11)
+    dev = [t.to(cuda_device) for t in (q, k, v, pose)]
+    out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
+    go = grad_out.to(cuda_device)
+    a = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05")
+    b = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05")
+    for x, y in zip(a[:4], b[:4]):
+        assert torch.equal(x, y)
+
+
+def test_fused_backward_partial_needs(cuda_device):
+    """Only the requested gradients: dQ and the pose gradient alone (the dK / dV
+    kernel is skipped), then dV alone."""
+    slots, q, k, v, pose, grad_out = _slot_case(10, 10, 8, 4, 2, 2, torch.bfloat16, seed=12)
+    dev = [t.to(cuda_device) for t in (q, k, v, pose)]
+    out, lse = look_attention_forward(*dev, slots, scale=0.125, want_lse=True)
+    go = grad_out.to(cuda_device)
+    full = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05")
+    part = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05",
+                                   needs=(True, False, False, True, False, False))
+    assert part[1] is None and part[2] is None
+    assert torch.equal(part[0], full[0]) and torch.equal(part[3], full[3])
+    only_v = look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05",
+                                     needs=(False, False, True, False, False, False))
+    assert only_v[0] is None and only_v[3] is None
+    assert torch.equal(only_v[2], full[2])
+
+
+def test_fused_backward_strided_qkv(cuda_device):
+    """q, k, v as head-split views of one fused qkv tensor (the model's layout)
+    through autograd: gradients against float64 autograd through the oracle."""
+    slots = LookSlots(hexgrid.synthetic_look_slots(12, 12, 8, 4), 32)
+    n = 145
+    gen = torch.Generator().manual_seed(13)
+    qkv = (torch.randn(2, n, 3, 3, 64, generator=gen) / 8).to(torch.bfloat16)
+    pose = torch.rand(2, n - 1, 3, 32, generator=gen) * 2 - 1
+    grad_out = torch.randn(2, 3, n, 64, generator=gen).to(torch.bfloat16)
+    qkv_d = qkv.to(cuda_device).requires_grad_(True)
+    pose_d = pose.to(cuda_device).requires_grad_(True)
+    q, k, v = qkv_d.permute(2, 0, 3, 1, 4).unbind(0)
+    out = structured_look_attention(q, k, v, pose_d, slots, scale=0.125)
+    out.backward(grad_out.to(cuda_device))
+    qkv_r = qkv.double().requires_grad_(True)
+    pose_r = pose.double().requires_grad_(True)
+    qr, kr, vr = qkv_r.permute(2, 0, 3, 1, 4).unbind(0)
+    ref = reference_structured_look_attention(qr, kr, vr, pose_r, _onehot_fields(slots, 3), scale=0.125)
+    ref.backward(grad_out.double())
+    for got, want in ((qkv_d.grad, qkv_r.grad), (pose_d.grad, pose_r.grad)):
+        err = (got.cpu().double() - want).abs().max().item()
+        assert err <= 2e-2 * max(want.abs().max().item(), 1e-3), err
 
 
 def test_tensor_core_backward_declines_other_inputs(cuda_device):

@@ -74,7 +74,7 @@ def test_svit_host_side_argument_checks():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.intp_abi_version() == 2
+    assert lib.intp_abi_version() == 3
     assert _lib.status_string(_lib.INTP_OK) == "ok"
     assert "timed out" in _lib.status_string(_lib.INTP_ERR_TIMEOUT)
 
