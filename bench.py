@@ -787,8 +787,8 @@ def run_ours(args) -> None:
             bwd_ms = max_over_ranks(statistics.mean(_timed_steps(lambda: work.backward_step(kind), args.steps,
                                                                  args.warmup, ctx, flush)), ctx)
             bwd_tflops = work.backward_flops / (bwd_ms * 1e-3) / 1e12
-            kernels = ("sla_bwd_pds_kernel (tcgen05: P, dS and the slot gradient) + 3 batched GEMMs "
-                       "(dQ, dK, dV; cuBLAS)" if kind == "auto" else
+            kernels = ("sla_bwd_dq_kernel + sla_bwd_dkdv_kernel (tcgen05; S, P, dP and dS recomputed "
+                       "on chip, dQ / dK / dV and the slot gradient accumulated in TMEM)" if kind == "auto" else
                        "delta_kernel + rows_kernel + cols_kernel (CUDA cores, fp32 accumulation)")
             extra[key] = {"kernels": kernels, "ms": round(bwd_ms, 4), "tflops": round(bwd_tflops, 3),
                           "flops": "algorithmic 10*B*H*N^2*D",
