@@ -537,7 +537,8 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const float2 xx = fma2(t[e], one2, nm2);
-            const float2 pe = make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
+            // a quarter of the pairs on the FMA pipe (exp2_fma), the rest on the MUFU
+            const float2 pe = (e & 3) == 3 ? exp2_fma(xx) : make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
             if (e & 1)
               acc1 = add2(acc1, pe);
             else

@@ -117,25 +117,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// mbar_wait without the suspend hint: the thread retries try_wait (which
-// blocks in hardware for a short, system-defined time) and resumes as soon as
-// the phase completes.  For single issuing threads on a critical path, where a
-// late wake-up costs more than the retries.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
-                                               int32_t* status, int32_t code, uint64_t budget_ns = kWaitBudgetNs) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (global_ns() - start > budget_ns) {
-      *abort = 1;
-      if (status) atomicCAS(status, 0, code);
-      return false;
-    }
-  }
-}
-
 // Makes this thread's earlier generic-proxy shared-memory writes visible to the
 // async proxy (TMA, tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_shared() {
@@ -332,6 +313,28 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for a pair on the FMA pipe instead of the MUFU (the kernels that are
+// bound by their exponentials run a share of them here, so both pipes work):
+// x = r + f with r = round(x) (adding 1.5 * 2^23 leaves r in the low mantissa
+// bits of t), 2^f for |f| <= 1/2 from a degree-3 polynomial whose coefficients
+// were fitted for relative error by iteratively reweighted least squares (at
+// most 7.5e-5, below half an ulp of a 16-bit result), then r added to the
+// exponent field (t << 23 equals r << 23 modulo 2^32).  x is clamped at -126
+// (keys masked with -inf included): 2^f may lie just below 1 (biased exponent
+// 126) and r >= -126 keeps the exponent field of the sum at 0 or above.
+__device__ __forceinline__ float2 exp2_fma(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = add2(x, make_float2(12582912.f, 12582912.f));
+  const float2 r = add2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = fma2(r, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(make_float2(0.05517202f, 0.05517202f), f, make_float2(0.24260995f, 0.24260995f));
+  p = fma2(p, f, make_float2(0.69326079f, 0.69326079f));
+  p = fma2(p, f, make_float2(0.99992812f, 0.99992812f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
