@@ -626,6 +626,28 @@ def _look_roofline(flops: float, per_launch_ms: float, peaks: dict, traffic, ker
             "launch_ms": round(per_launch_ms, 5), "where": where}
 
 
+def _model_attention_roofline(batch: int, per_launch_ms: float, peaks: dict, traffic, where: str) -> dict:
+    """The Look attention on the model's inputs (B x 3 heads x 196 tokens, D 64).
+
+    Its arithmetic intensity, 4*B*H*N^2*D FLOPs over the algorithmic bytes
+    (q, k, v and the output in bf16, the (B, 195, 3, 12) fp32 Look pose), is
+    about 90 FLOP/byte: below the measured ridge point (bf16 peak / HBM
+    bandwidth, about 251 FLOP/byte), so HBM is the roof.  The tensor-core
+    fraction is reported beside it."""
+    flops = 4.0 * batch * 3 * 196 * 196 * 64
+    algo_bytes = 3 * batch * 3 * 196 * 64 * 2 + batch * 195 * 3 * 12 * 4 + batch * 3 * 196 * 64 * 2
+    sec = per_launch_ms * 1e-3
+    gbs, tflops = algo_bytes / sec / 1e9, flops / sec / 1e12
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": traffic, "kernel": "sla_short_kernel",
+            "peak_source": f"{peaks['source']} HBM copy bandwidth", "launch_ms": round(per_launch_ms, 5),
+            "algorithmic_bytes": algo_bytes, "flops": flops,
+            "intensity_flop_per_byte": round(flops / algo_bytes, 1), "ridge_flop_per_byte": round(ridge, 1),
+            "tensor_achieved_tflops": round(tflops, 2), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
+            "where": where}
+
+
 def _nl1_roofline(work, per_launch_ms: float, peaks: dict) -> dict:
     """negative-L1: GB/s against HBM as asked, and beside it the op rate
     against the FP32 lanes' rate at the maximum SM clock (148 SMs x 128
@@ -735,13 +757,10 @@ def run_ours(args) -> None:
         # arguments of one forward, replayed as one CUDA graph of 12 launches
         # (no host gaps), CUDA events around each replay, L2 flushed before it.
         attn_ms = _model_attention_ms(work, args, ctx, flush)
-        flops = 4.0 * work.batch * 3 * 196 * 196 * 64
-        roofline = _look_roofline(flops, attn_ms, peaks,
-                                  MODEL_ATTN_TRAFFIC_BYTES if work.batch == 256 else None,
-                                  "sla_short_kernel",
-                                  f"Look attention on the model forward's inputs (B{work.batch} H3 N196 D64 bf16, "
-                                  "68 slots, SLOT_FIELDS), the 12 layers' launches replayed as one CUDA graph, "
-                                  "per launch")
+        roofline = _model_attention_roofline(
+            work.batch, attn_ms, peaks, MODEL_ATTN_TRAFFIC_BYTES if work.batch == 256 else None,
+            f"Look attention on the model forward's inputs (B{work.batch} H3 N196 D64 bf16, 68 slots, SLOT_FIELDS), "
+            "the 12 layers' launches replayed as one CUDA graph, per launch")
         # ours per step: hex gather + post-GEMM + the first LayerNorm, then per block
         # qkv, Look attention, proj + residual + LN, fc1 + GELU, fc2 + residual + LN
         # (the tokenizer GEMM and the classifier head are cuBLAS)
