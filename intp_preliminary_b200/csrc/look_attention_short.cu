@@ -61,7 +61,8 @@ struct alignas(8) ShortBars {
   uint64_t o_full[2];             // O_x computed
   uint64_t o_free[2];             // O_x read by the epilogue: region x may be overwritten (4 Look warps)
   uint64_t sf_ready[2];           // SLOT_FIELDS: an item's slot values staged in buffer b (4 Look warps)
-  uint64_t sf_free[2];            // both tables built from buffer b (4 warps per query tile)
+  uint64_t p1_done[2];            // softmax x finished pass 1: its Look table may be rebuilt (4 warps)
+  uint64_t tab_full[2];           // the Look warpgroup built table x for the next item (4 Look warps)
   uint64_t stagger;               // tile A finished its first pass 1 (4 softmax warps): tile B starts
   uint64_t drain[2];
   uint32_t tmem_base;
@@ -256,7 +257,8 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_init(&bars->o_full[x], 1);
       mbar_init(&bars->o_free[x], 4);
       mbar_init(&bars->sf_ready[x], 4);
-      mbar_init(&bars->sf_free[x], 4 * nt);
+      mbar_init(&bars->p1_done[x], 4);
+      mbar_init(&bars->tab_full[x], 4);
     }
     mbar_init(&bars->stagger, 4);
     mbar_init(&bars->drain[0], 1);
@@ -393,31 +395,14 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if ((p.slot_tile_flags[x * a.n_kt + kt] >> qw) & 1) bias_tiles |= 1u << kt;
     bool ok = x < nt;
     if (ok && use_bias) ok = mbar_wait(&bars->slots_full, 0, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns);
-    // This warpgroup's table for item `it` (the kk-th of this CTA): SLOTS copies
-    // the rows' Look values, SLOT_FIELDS forms pose x slot values from the
-    // staging buffer kk & 1 (staged by the Look warpgroup).
-    float* tab = table_s + x * a.table_floats;
-    auto build = [&](uint32_t kk, uint32_t it) -> bool {
-      const uint32_t h = it % H, b = it / H;
-      if (!a.slot_fields) {
-        stage_table(tab, a, b, h, tok, row);
-        __syncwarp();
-        return true;
-      }
-      float w[kMaxLookPoses];
-      load_pose_row(w, a, b, h, tok);
-      const uint32_t sb = kk & 1;
-      if (a.sf_vec4 && !mbar_wait(&bars->sf_ready[sb], (kk >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax,
-                                  a.wait_ns))
-        return false;
-      build_table_sf(tab, sf_s + sb * a.sf_floats, a, h, row, w);
-      __syncwarp();
-      if (a.sf_vec4 && lane == 0) mbar_arrive(&bars->sf_free[sb]);
-      return true;
-    };
     uint32_t k = 0;
-    if (ok && use_bias && blockIdx.x < n_items) ok = build(0, blockIdx.x);
     for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++k) {
+      // The item's Look table, built by the Look warpgroup while this
+      // warpgroup ran pass 2 of the previous item.
+      if (use_bias && !mbar_wait(&bars->tab_full[x], k & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) {
+        ok = false;
+        break;
+      }
       if (!mbar_wait(&bars->s_full[x], k & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) {
         ok = false;
         break;
@@ -513,7 +498,10 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tmem_wait_st();
       }
       __syncwarp();
-      if (x == 0 && k == 0 && nt == 2 && lane == 0) mbar_arrive(&bars->stagger);
+      if (lane == 0) {
+        if (use_bias) mbar_arrive(&bars->p1_done[x]);  // table reads of this item are done
+        if (x == 0 && k == 0 && nt == 2) mbar_arrive(&bars->stagger);
+      }
       if (warp_live) {
         // pass 2: P = 2^(logit - m), row sum, 16-bit pairs over the first kr/2 columns
         const float2 nm2 = make_float2(-m, -m), one2 = make_float2(1.f, 1.f);
@@ -566,11 +554,6 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[x]);
-      // The next item's table, while PV, the epilogue and the next S MMA run.
-      if (use_bias && item + gridDim.x < n_items && !build(k + 1, item + gridDim.x)) {
-        ok = false;
-        break;
-      }
     }
   } else if (warp < 12) {
     // ------------------------------------------------------------ Look warpgroup
@@ -623,27 +606,61 @@ sla_short_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       return true;
     };
-    // Slot values (SLOT_FIELDS) of the CTA's kk-th item into buffer kk & 1,
-    // once both tables of item kk - 2 were built from it.
+    // Slot values (SLOT_FIELDS) of the CTA's kk-th item into buffer kk & 1.
+    // Its previous contents (item kk - 2) were read by this warpgroup's own
+    // table builds for that item, which every Look warp finished before the
+    // softmax could start that item's pass 1 (tab_full) - long before any Look
+    // warp gets here, past the epilogues of item kk - 2.
     const bool stage = use_bias && a.slot_fields && a.sf_vec4;
-    auto stage_sf = [&](uint32_t kk, uint32_t it) -> bool {
-      const uint32_t sb = kk & 1;
-      if (kk >= 2 && !mbar_wait(&bars->sf_free[sb], ((kk >> 1) - 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax,
-                                a.wait_ns))
-        return false;
-      stage_slot_fields(sf_s + sb * a.sf_floats, a, it % H, lt, QM);
+    auto stage_sf = [&](uint32_t kk, uint32_t it) {
+      stage_slot_fields(sf_s + (kk & 1) * a.sf_floats, a, it % H, lt, QM);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sf_ready[sb]);
+      if (lane == 0) mbar_arrive(&bars->sf_ready[kk & 1]);
+    };
+    // Table x of the CTA's kk-th item (`it`): SLOTS copies the rows' Look
+    // values, SLOT_FIELDS forms pose x slot values (each warp its 32 rows,
+    // the rows softmax warp qw of tile x reads).
+    // SLOT_FIELDS: the pose rows of the next item's two tiles, loaded at the
+    // top of an iteration so their memory latency passes while this warpgroup
+    // waits for the softmax; `build` consumes them.
+    auto build = [&](int x, uint32_t kk, uint32_t it) -> bool {
+      const uint32_t h = it % H, b = it / H;
+      const int32_t tok = x * QM + lt;
+      float* tab = table_s + x * a.table_floats;
+      if (!a.slot_fields) {
+        stage_table(tab, a, b, h, tok, lt);
+      } else {
+        float w[kMaxLookPoses];
+        load_pose_row(w, a, b, h, tok);
+        if (a.sf_vec4 && !mbar_wait(&bars->sf_ready[kk & 1], (kk >> 1) & 1, abort_flag, p.status,
+                                    kDevTimeoutSoftmax, a.wait_ns))
+          return false;
+        build_table_sf(tab, sf_s + (kk & 1) * a.sf_floats, a, h, lt, w);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tab_full[x]);
       return true;
     };
     uint32_t k = 0;
-    if (stage && blockIdx.x < n_items) ok = stage_sf(0, blockIdx.x);
+    if (use_bias && blockIdx.x < n_items) {
+      if (stage) stage_sf(0, blockIdx.x);
+      for (int x = 0; x < nt && ok; ++x) ok = build(x, 0, blockIdx.x);
+    }
     for (uint32_t item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++k) {
-      if (stage && item + gridDim.x < n_items && !stage_sf(k + 1, item + gridDim.x)) {
-        ok = false;
-        break;
+      const uint32_t next = item + gridDim.x;
+      if (stage && next < n_items) stage_sf(k + 1, next);
+      for (int x = 0; x < nt && ok; ++x) {
+        // Table x of the next item once softmax x is through pass 1 of this one
+        // (it runs pass 2, the PV MMA and this epilogue meanwhile).
+        if (use_bias && next < n_items) {
+          if (!mbar_wait(&bars->p1_done[x], k & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns) ||
+              !build(x, k + 1, next)) {
+            ok = false;
+            break;
+          }
+        }
+        ok = epilogue(k, item, x);
       }
-      for (int x = 0; x < nt && ok; ++x) ok = epilogue(k, item, x);
     }
   }
 
