@@ -50,10 +50,10 @@ sys.path.insert(0, str(ROOT))
 
 # DRAM bytes (read + write) of one sla_tc_kernel launch at look_cfg4, from one
 # ncu capture of that launch (dram__bytes_read.sum + dram__bytes_write.sum).
-CFG4_TRAFFIC_BYTES = int((202.120704 + 33.865216) * 1e6)
+CFG4_TRAFFIC_BYTES = int((202.150400 + 34.622976) * 1e6)
 # DRAM bytes (read + write) of one sla_short_kernel launch on the model forward's
 # inputs (B256 H3 N196, SLOT_FIELDS), from one ncu capture of that launch.
-MODEL_ATTN_TRAFFIC_BYTES = int((70.782208 + 2.970112) * 1e6)
+MODEL_ATTN_TRAFFIC_BYTES = int((70.775808 + 3.503360) * 1e6)
 # DRAM bytes (read + write) of one nl1_vec_kernel launch (50176 x 576 x F), from
 # one ncu capture per feature size.
 NL1_TRAFFIC_BYTES = {1728: int((350.991872 + 97.320448) * 1e6), 432: int((87.734528 + 71.396864) * 1e6)}
