@@ -16,6 +16,8 @@
  *                         Look bank's null softmax (layers/square_patch_dense_grid_look.py:339-355)
  *                         contracted with the per-slot Look fields into the
  *                         per-query Look values the attention kernel reads.
+ *   svit_tokenizer_gemm : that GEMM with svit_embed_post's softmaxes in its
+ *                         epilogue (tcgen05; the response matrix is never stored).
  *   svit_add_layernorm  : residual add + LayerNorm + bf16 cast of the
  *                         pre-norm transformer block (layers/mini_vit.py:138-170).
  *   svit_linear_gelu,   : the block's linear layers on tcgen05 with GELU, or
@@ -97,6 +99,26 @@ typedef struct svit_embed_args {
 } svit_embed_args;
 
 INTP_API intp_status svit_embed_post(const svit_embed_args* args, void* stream);
+
+/* The tokenizer + Look-bank GEMM and svit_embed_post's work in one tcgen05
+ * kernel (replaces the reference's rotating-dot responses and the softmaxes
+ * that follow them, layers/hex_rotating_harmonic_patch_embed.py:153-242 and
+ * layers/square_patch_dense_grid_look.py:339-355): C = patches W^T with fp32
+ * accumulators in tensor memory, and from them, without writing C,
+ *   x[b, n+1, 2p + c] = sum_d softmax_d,null(C[., 6p + d]) coef[d, c]
+ *                       + output_bias[2p + c] + pos_embed[n+1, 2p + c],
+ *   x[b, 0] = cls + pos_embed[0],
+ *   look_pose[b, n, h, pp] = softmax_pp,null(C[., 6 bases + 12 h + pp]).
+ * patches: (batch * args->patches, features) bf16, row stride patches_stride
+ * (16-byte aligned rows); weight: (6 bases + 12 look_heads, features) bf16
+ * contiguous, the tokenizer rows first, then the Look rows head by head (head
+ * h's 12 poses consecutive).  args: directions == 6, look_poses == 12,
+ * bases % 24 == 0, look_heads % 12 == 0, values == NULL, x and look_pose set;
+ * resp and slot_fields are not used.  features % 8 == 0 (a ragged last
+ * 64-wide K slab reads zeros).  `status`: the device int32 of the bounded
+ * waits (as in sla_forward_args.status).                                     */
+INTP_API intp_status svit_tokenizer_gemm(const svit_embed_args* args, const void* patches, int64_t patches_stride,
+                                         int32_t features, const void* weight, int32_t* status, void* stream);
 
 /* For r < rows: x[r] += y[r] (when y is not NULL; y bf16), then
  * h[r] = bf16(LayerNorm(x[r]) * gamma + beta) over `dim` features.

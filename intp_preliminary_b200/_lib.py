@@ -52,6 +52,7 @@ SHARE_VIT_SYMBOLS = (
     "svit_gather_patches",
     "svit_gather_patches_staged",
     "svit_embed_post",
+    "svit_tokenizer_gemm",
     "svit_add_layernorm",
     "svit_linear_gelu",
     "svit_linear_bias",
@@ -216,6 +217,8 @@ def load() -> ctypes.CDLL:
         lib.svit_gather_patches_staged.restype = _i32
         lib.svit_embed_post.argtypes = [ctypes.POINTER(SvitEmbedArgs), _vp]
         lib.svit_embed_post.restype = _i32
+        lib.svit_tokenizer_gemm.argtypes = [ctypes.POINTER(SvitEmbedArgs), _vp, _i64, _i32, _vp, _vp, _vp]
+        lib.svit_tokenizer_gemm.restype = _i32
         lib.svit_add_layernorm.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, ctypes.c_float, _i64, _i64, _vp, _i64, _vp]
         lib.svit_add_layernorm.restype = _i32
         lib.svit_linear_gelu.argtypes = [_vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp]

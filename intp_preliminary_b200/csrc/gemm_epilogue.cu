@@ -5,6 +5,11 @@
 //   GELU epilogue:      out = bf16(GELU_erf(C))                       (MLP fc1)
 //   bias epilogue:      out = bf16(C)                                  (attention qkv)
 //   residual + LN:      x += C (fp32);  h = bf16(LayerNorm(x))         (attention proj, MLP fc2)
+//   tokenizer:          the patch tokenizer's and the Look bank's null softmaxes straight
+//                       from the fp32 accumulators (no response matrix in memory):
+//                       tokens x (harmonic moments + bias + position, CLS row) and the
+//                       Look pose, layers/hex_rotating_harmonic_patch_embed.py:153-242 and
+//                       layers/square_patch_dense_grid_look.py:339-355
 // so the MLP's 768-wide activation is written once (by fc1, already
 // activated) and the residual stream is read and written once per sub-block,
 // with no separate GELU or add + LayerNorm pass (layers/mini_vit.py:138-170).
@@ -34,13 +39,13 @@ constexpr uint32_t kASlab = kGBM * kGBK * 2;       // 16 KB
 // accumulator buffer for GELU (each takes half of the tile's columns), one for
 // LayerNorm (a row's statistics stay inside one thread).
 template <int EPI>
-__host__ __device__ constexpr int epi_groups_per_tile() { return EPI == 1 ? 1 : 2; }
+__host__ __device__ constexpr int epi_groups_per_tile() { return EPI == 1 || EPI == 3 ? 1 : 2; }
 template <int EPI>
 __host__ __device__ constexpr int gemm_threads() { return 64 + 2 * epi_groups_per_tile<EPI>() * 128; }
-constexpr int kEpiGelu = 0, kEpiResidualLN = 1, kEpiBias = 2;
+constexpr int kEpiGelu = 0, kEpiResidualLN = 1, kEpiBias = 2, kEpiTokenizer = 3;
 // Per epilogue warp, in 32-bit words: GELU two 32 x 32 bf16 blocks; LN two 32 x 32 fp32 residual chunks.
 template <int EPI>
-__host__ __device__ constexpr int stage_words() { return EPI == 1 ? 2048 : 1024; }
+__host__ __device__ constexpr int stage_words() { return EPI == 3 ? 0 : (EPI == 1 ? 2048 : 1024); }
 constexpr int kMaxGeluN = 4096;         // GELU bias columns kept in shared memory
 constexpr uint32_t kBarrierBytes = 256;  // room reserved for the barrier block
 
@@ -60,6 +65,18 @@ struct GemmArgs {
   __nv_bfloat16* h;    // LN: output (M, N) bf16, row stride h_stride
   int64_t h_stride;
   int32_t* status;
+  // tokenizer epilogue (EPI 3): rows are (image, patch) pairs; tiles 0 .. tok_tiles-1
+  // cover the tokenizer's bases, the rest the Look bank's heads
+  int32_t patches;             // patches per image
+  int32_t tok_tiles;           // N-tiles of tokenizer columns
+  const float* token_null;     // (bases)
+  const float* direction_coef; // (6, 2)
+  const float* output_bias;    // (2 bases)
+  const float* cls;            // (2 bases)
+  const float* pos_embed;      // (patches + 1, 2 bases)
+  const float* look_null;      // (look heads)
+  float* look_pose;            // (rows, look heads, 12)
+  int32_t look_heads;
 };
 
 template <int STAGES>
@@ -378,6 +395,95 @@ __device__ __forceinline__ void epilogue_residual_ln(uint32_t acc, const float* 
   __syncwarp();
 }
 
+// Tokenizer epilogue of one warp (32 rows = lanes) on a 144-column tile: 24
+// tokenizer bases x 6 directions, or 12 Look heads x 12 poses (the weight's
+// Look rows are ordered head by head).  48 columns (8 bases / 4 heads) per
+// step; the accumulator is released once its last columns are loaded.
+//   base p: s_d = C[6p + d], null n_p: e_d = exp(s_d - m), m = max(n_p, s),
+//     x[2p + c] = sum_d e_d coef[d, c] / (exp(n_p - m) + sum_d e_d) + bias + pos
+//   head h: pose[pp] = exp(s_pp - m) / (exp(n_h - m) + sum exp(s - m))
+// (the null state's share is dropped, as in the reference).
+constexpr int kTokDirs = 6, kLookPoses = 12, kTokTileN = 144;
+__device__ __forceinline__ void epilogue_tokenizer(uint32_t acc, int64_t tile_n, int64_t m, const GemmArgs& g,
+                                                   int lane, uint64_t* acc_empty) {
+  const bool valid = m < g.M;
+  const int64_t img = valid ? m / g.patches : 0, n = valid ? m - img * g.patches : 0;
+  const bool tok = tile_n < g.tok_tiles;
+  const int dim = 2 * static_cast<int>(g.tok_tiles) * (kTokTileN / kTokDirs);  // 2 * bases
+#pragma unroll 1
+  for (int st = 0; st < 3; ++st) {
+    uint32_t r0[16], r1[16], r2[16];
+    tmem_ld16(acc + 48 * st, r0);
+    tmem_ld16(acc + 48 * st + 16, r1);
+    tmem_ld16(acc + 48 * st + 32, r2);
+    tmem_wait_ld();
+    reg_fence16(r0);
+    reg_fence16(r1);
+    reg_fence16(r2);
+    if (st == 2) release_acc(acc_empty, lane);
+    float v[48];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      v[e] = __uint_as_float(r0[e]);
+      v[16 + e] = __uint_as_float(r1[e]);
+      v[32 + e] = __uint_as_float(r2[e]);
+    }
+    if (!valid) continue;
+    if (tok) {
+      const int p0 = static_cast<int>(tile_n) * (kTokTileN / kTokDirs) + 8 * st;  // first base of the step
+      float* xrow = g.x + (img * (g.patches + 1) + n + 1) * dim;
+      const float* pos = g.pos_embed + (n + 1) * dim;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int p = p0 + i;
+        const float nul = __ldg(g.token_null + p);
+        float mx = nul;
+#pragma unroll
+        for (int d = 0; d < kTokDirs; ++d) mx = fmaxf(mx, v[kTokDirs * i + d]);
+        float sum = __expf(nul - mx), tx = 0.f, ty = 0.f;
+#pragma unroll
+        for (int d = 0; d < kTokDirs; ++d) {
+          const float e = __expf(v[kTokDirs * i + d] - mx);
+          sum += e;
+          tx = fmaf(e, __ldg(g.direction_coef + 2 * d), tx);
+          ty = fmaf(e, __ldg(g.direction_coef + 2 * d + 1), ty);
+        }
+        const float inv = 1.f / sum;
+        *reinterpret_cast<float2*>(xrow + 2 * p) =
+            make_float2(fmaf(tx, inv, __ldg(g.output_bias + 2 * p) + __ldg(pos + 2 * p)),
+                        fmaf(ty, inv, __ldg(g.output_bias + 2 * p + 1) + __ldg(pos + 2 * p + 1)));
+      }
+      if (n == 0) {  // this image's CLS row, the same 16 columns
+        float* crow = g.x + img * (g.patches + 1) * dim;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) crow[2 * p0 + c] = __ldg(g.cls + 2 * p0 + c) + __ldg(g.pos_embed + 2 * p0 + c);
+      }
+    } else {
+      const int h0 = static_cast<int>(tile_n - g.tok_tiles) * (kTokTileN / kLookPoses) + 4 * st;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int hh = h0 + i;
+        const float nul = __ldg(g.look_null + hh);
+        float mx = nul;
+#pragma unroll
+        for (int pp = 0; pp < kLookPoses; ++pp) mx = fmaxf(mx, v[kLookPoses * i + pp]);
+        float e[kLookPoses];
+        float sum = __expf(nul - mx);
+#pragma unroll
+        for (int pp = 0; pp < kLookPoses; ++pp) {
+          e[pp] = __expf(v[kLookPoses * i + pp] - mx);
+          sum += e[pp];
+        }
+        const float inv = 1.f / sum;
+        float4* dst = reinterpret_cast<float4*>(g.look_pose + (m * g.look_heads + hh) * kLookPoses);
+#pragma unroll
+        for (int c = 0; c < kLookPoses / 4; ++c)
+          dst[c] = make_float4(e[4 * c] * inv, e[4 * c + 1] * inv, e[4 * c + 2] * inv, e[4 * c + 3] * inv);
+      }
+    }
+  }
+}
+
 template <int NT, int STAGES, int EPI>
 __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -413,7 +519,7 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const int n_slabs = g.K / kGBK;
+  const int n_slabs = (g.K + kGBK - 1) / kGBK;  // a ragged last slab reads zeros past K
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -499,7 +605,9 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     float* sparams = reinterpret_cast<float*>(smem + STAGES * kStage + kBarrierBytes +
                                               8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4);
     if (threadIdx.x == 64) {
-      if (EPI != kEpiResidualLN) {
+      if (EPI == kEpiTokenizer) {
+        mbar_arrive(&bars->params);  // no parameter copy: the epilogue reads them through L1
+      } else if (EPI != kEpiResidualLN) {
         mbar_arrive_expect_tx(&bars->params, static_cast<uint32_t>(g.N) * 4u);
         bulk_load(sparams, g.bias, static_cast<uint32_t>(g.N) * 4u, &bars->params);
       } else {
@@ -524,7 +632,14 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       const int32_t n0 = static_cast<int32_t>((t % g.n_tiles_n) * NT);
       const uint32_t acc = lane_base + e * NT + col0;
       const int64_t wrow0 = (t / g.n_tiles_n) * kGBM + (warp & 3) * 32;  // first row of this warp
-      if (EPI != kEpiResidualLN) {
+      if (EPI == kEpiTokenizer) {
+        if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        epilogue_tokenizer(acc, t % g.n_tiles_n, wrow0 + lane, g, lane, &bars->acc_empty[e]);
+      } else if (EPI != kEpiResidualLN) {
         if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
           ok = false;
           break;
@@ -596,7 +711,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 template <int NT, int STAGES, int EPI>
 intp_status launch_gemm(const void* a, int64_t a_stride, const void* w, GemmArgs g, cudaStream_t stream) {
-  if (g.K % kGBK || g.N % NT) return INTP_ERR_SHAPE;
+  if ((EPI != kEpiTokenizer && g.K % kGBK) || g.K % 8 || g.N % NT) return INTP_ERR_SHAPE;
   if (!aligned16(a) || !aligned16(w) || (a_stride * 2) % 16) return INTP_ERR_LAYOUT;
   CUtensorMap ma, mb;
   if (!make_map_2d(&ma, a, g.M, g.K, a_stride, kGBM) || !make_map_2d(&mb, w, g.N, g.K, g.K, NT))
@@ -609,7 +724,7 @@ intp_status launch_gemm(const void* a, int64_t a_stride, const void* w, GemmArgs
     return INTP_ERR_LAUNCH;
   auto kernel = gemm_epilogue_kernel<NT, STAGES, EPI>;
   static_assert(sizeof(GemmBarriers<STAGES>) <= kBarrierBytes, "barrier block");
-  const size_t params = EPI != kEpiResidualLN ? static_cast<size_t>(g.N) : 3 * NT;
+  const size_t params = EPI == kEpiTokenizer ? 0 : (EPI != kEpiResidualLN ? static_cast<size_t>(g.N) : 3 * NT);
   const size_t smem = 1024 + STAGES * (kASlab + NT * kGBK * 2) + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4 + params * 4;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
@@ -700,4 +815,39 @@ extern "C" INTP_API intp_status svit_linear_residual_layernorm(const void* a, in
   g.h_stride = h_stride;
   g.status = status;
   return launch_gemm<192, 3, kEpiResidualLN>(a, a_stride, weight, g, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" INTP_API intp_status svit_tokenizer_gemm(const svit_embed_args* args, const void* patches,
+                                                    int64_t patches_stride, int32_t features, const void* weight,
+                                                    int32_t* status, void* stream) {
+  if (!args || !patches || !weight || !status) return INTP_ERR_ARGUMENT;
+  const svit_embed_args& a = *args;
+  if (a.batch < 0 || a.patches < 1 || features < 8) return INTP_ERR_SHAPE;
+  if (a.batch == 0) return INTP_OK;
+  if (a.directions != kTokDirs || a.look_poses != kLookPoses || a.bases % (kTokTileN / kTokDirs) ||
+      a.look_heads % (kTokTileN / kLookPoses) || a.bases < 1 || a.look_heads < 1)
+    return INTP_ERR_UNSUPPORTED;
+  if (a.values != nullptr || !a.look_pose || !a.x || !a.token_null || !a.direction_coef || !a.output_bias || !a.cls ||
+      !a.pos_embed || !a.look_null)
+    return INTP_ERR_ARGUMENT;
+  if (features % 8 || patches_stride < features || !aligned16(a.look_pose)) return INTP_ERR_LAYOUT;
+  if (!device_is_sm100()) return INTP_ERR_ARCH;
+  GemmArgs g{};
+  g.M = a.batch * a.patches;
+  g.N = a.bases * kTokDirs + a.look_heads * kLookPoses;
+  g.K = features;
+  g.x = a.x;
+  g.status = status;
+  g.patches = static_cast<int32_t>(a.patches);
+  g.tok_tiles = a.bases * kTokDirs / kTokTileN;
+  g.token_null = a.token_null;
+  g.direction_coef = a.direction_coef;
+  g.output_bias = a.output_bias;
+  g.cls = a.cls;
+  g.pos_embed = a.pos_embed;
+  g.look_null = a.look_null;
+  g.look_pose = a.look_pose;
+  g.look_heads = a.look_heads;
+  return launch_gemm<kTokTileN, 4, kEpiTokenizer>(patches, patches_stride, weight, g,
+                                                   static_cast<cudaStream_t>(stream));
 }

@@ -53,7 +53,7 @@ import torch.nn.functional as F
 
 from .look_attention import LookSlotFields, LookSlots, look_attention_forward
 from .share_vit_ops import (GatherPlan, add_layernorm, embed_post, gather_patches, gather_plan, linear_bias,
-                            linear_gelu, linear_residual_layernorm)
+                            linear_gelu, linear_residual_layernorm, tokenizer_gemm)
 
 IMAGE_SIZE = 224
 IN_CHANS = 3
@@ -477,8 +477,31 @@ class ShareViTHalf6d3r(nn.Module):
             self._cache[key] = hit
         return hit
 
+    def _tokenizer_weights(self, device):
+        """The fused GEMM's weight with the Look rows ordered head by head: row
+        576 + 12 h + 6 s + d holds support s's direction-d response of Look head h
+        (in ``_fused_embed_weights`` it is row 576 + 216 s + 6 h + d), so one
+        head's 12 poses are 12 consecutive accumulator columns."""
+        w, fields = self._fused_embed_weights(device)
+        key = ("tokenizer", device, self._weights_key())
+        with self._cache_lock:
+            hit = self._cache.get(key)
+        if hit is not None:
+            return hit, fields
+        tok = BASES * DIRECTIONS
+        h = torch.arange(LOOK_HEADS).view(-1, 1, 1)
+        s_ = torch.arange(2).view(1, -1, 1)
+        d = torch.arange(DIRECTIONS).view(1, 1, -1)
+        look_rows = (tok + s_ * LOOK_HEADS * DIRECTIONS + h * DIRECTIONS + d).reshape(-1)
+        order = torch.cat((torch.arange(tok), look_rows)).to(device)
+        hit = w.index_select(0, order).contiguous()
+        with self._cache_lock:
+            self._cache = {k: v for k, v in self._cache.items() if k[0] != "tokenizer"}
+            self._cache[key] = hit
+        return hit, fields
+
     @torch.no_grad()
-    def embed_fused(self, image: torch.Tensor, *, per_slot_values: bool = False):
+    def embed_fused(self, image: torch.Tensor, *, per_slot_values: bool = False, fused_tokenizer: bool = True):
         """bf16 tokenizer + Look bank on the fused kernels: the residual stream
         x (B, N+1, 192) fp32 with CLS and position embedding, and the Look
         inputs of the 12 attention layers.  Default: a ``LookPose`` - the Look
@@ -495,8 +518,22 @@ class ShareViTHalf6d3r(nn.Module):
         plan = GatherPlan(self.gather_stage_offset, self.gather_stage_begin, self.gather_local_index,
                           *self._gather_plan_sizes)
         patches = gather_patches(image, self.pixel_index, self.pixel_weight, plan=plan)
-        resp = patches @ w.t()
         x = torch.empty(batch, n + 1, EMBED_DIM, dtype=torch.float32, device=image.device)
+        if fused_tokenizer and not per_slot_values:
+            # one tcgen05 kernel: the GEMM and the softmaxes from its fp32 accumulators
+            wt, _ = self._tokenizer_weights(image.device)
+            look_pose = torch.empty(batch, n, LOOK_HEADS, 2 * DIRECTIONS, dtype=torch.float32, device=image.device)
+            tokenizer_gemm(patches, wt, batch=batch, patches_per_image=n, bases=BASES, directions=DIRECTIONS,
+                           look_heads=LOOK_HEADS, look_poses=2 * DIRECTIONS,
+                           token_null=self.patch_embed.null_score.detach().float().contiguous(),
+                           direction_coef=self.direction_coefficients.contiguous(),
+                           output_bias=self.patch_embed.output_bias.detach().float().contiguous(),
+                           cls=self.cls_token.detach().float().reshape(-1).contiguous(),
+                           pos_embed=self.pos_embed.detach().float().reshape(n + 1, EMBED_DIM).contiguous(),
+                           look_null=self.look_bank.null_score.detach().float().contiguous(), x=x,
+                           look_pose=look_pose)
+            return x, LookPose(look_pose, fields)
+        resp = patches @ w.t()
         values = look_pose = None
         if per_slot_values:
             values = torch.empty(batch, LOOK_HEADS, n, fields.shape[-1], dtype=torch.float32, device=image.device)

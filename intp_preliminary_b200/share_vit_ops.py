@@ -160,6 +160,42 @@ def embed_post(resp: torch.Tensor, *, batch: int, patches: int, bases: int, dire
     _lib.check(status, "tokenizer / Look-bank post-processing")
 
 
+def tokenizer_gemm(patches: torch.Tensor, weight: torch.Tensor, *, batch: int, patches_per_image: int, bases: int,
+                   directions: int, look_heads: int, look_poses: int, token_null: torch.Tensor,
+                   direction_coef: torch.Tensor, output_bias: torch.Tensor, cls: torch.Tensor, pos_embed: torch.Tensor,
+                   look_null: torch.Tensor, x: torch.Tensor, look_pose: torch.Tensor) -> None:
+    """The tokenizer + Look-bank GEMM with ``embed_post``'s softmaxes in its
+    epilogue (one tcgen05 kernel; the response matrix is never stored):
+    tokens into ``x`` (B, N+1, 2*bases) and the Look pose into ``look_pose``
+    (B, N, look_heads, look_poses) from the bf16 ``patches`` (B*N, F) and the
+    bf16 ``weight`` (bases*directions + look_heads*look_poses, F) whose Look
+    rows are ordered head by head."""
+    dev = patches.device
+    _require(patches.is_cuda and patches.dtype == torch.bfloat16 and patches.ndim == 2 and patches.stride(1) == 1,
+             "patches must be a bf16 CUDA matrix with unit column stride")
+    _require(patches.shape[0] == batch * patches_per_image, "patches must have batch * patches_per_image rows")
+    rows_w = bases * directions + look_heads * look_poses
+    _require(weight.device == dev and weight.dtype == torch.bfloat16 and weight.is_contiguous()
+             and tuple(weight.shape) == (rows_w, patches.shape[1]),
+             "weight must be a contiguous bf16 (bases*directions + look_heads*look_poses, F) matrix")
+    for t in (token_null, direction_coef, output_bias, cls, pos_embed, look_null, x, look_pose):
+        _require(t.device == dev and t.dtype == torch.float32 and t.is_contiguous(),
+                 "parameters and outputs must be contiguous float32 tensors on the patches' device")
+    _require(x.shape == (batch, patches_per_image + 1, 2 * bases), "x must be (B, N+1, 2*bases)")
+    _require(look_pose.shape == (batch, patches_per_image, look_heads, look_poses),
+             "look_pose must be (B, N, look_heads, look_poses)")
+    a = _lib.SvitEmbedArgs()
+    a.batch, a.patches = batch, patches_per_image
+    a.bases, a.directions, a.look_heads, a.look_poses, a.slots = bases, directions, look_heads, look_poses, 0
+    a.token_null, a.direction_coef, a.output_bias = token_null.data_ptr(), direction_coef.data_ptr(), output_bias.data_ptr()
+    a.cls, a.pos_embed, a.look_null = cls.data_ptr(), pos_embed.data_ptr(), look_null.data_ptr()
+    a.x, a.values, a.look_pose = x.data_ptr(), None, look_pose.data_ptr()
+    status = _lib.load().svit_tokenizer_gemm(ctypes.byref(a), ctypes.c_void_p(patches.data_ptr()), patches.stride(0),
+                                             patches.shape[1], ctypes.c_void_p(weight.data_ptr()),
+                                             _status(dev), _stream(dev))
+    _lib.check(status, "fused tokenizer / Look-bank GEMM")
+
+
 def add_layernorm(x: torch.Tensor, y: torch.Tensor | None, weight: torch.Tensor, bias: torch.Tensor, eps: float,
                   out: torch.Tensor | None = None) -> torch.Tensor:
     """``x += y`` (when given, in place) then ``out = bf16(LayerNorm(x))`` over the last dim.

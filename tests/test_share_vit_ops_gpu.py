@@ -95,12 +95,69 @@ def test_embed_fused_matches_unfused(model, cuda_device):
     torch.testing.assert_close(x, ref_x, atol=3e-2, rtol=3e-2)
     torch.testing.assert_close(values, ref_values, atol=3e-2, rtol=3e-2)
     assert torch.equal(x[:, 0], (model.cls_token[0, 0] + model.pos_embed[0, 0]).expand(4, -1))
-    # default: the Look pose and slot values instead of their product
+    # default: the Look pose and slot values instead of their product, from the
+    # fused tokenizer GEMM (fp32 scores instead of the bf16 response matrix)
     x2, look = model.embed_fused(images)
     assert isinstance(look, LookPose)
-    torch.testing.assert_close(x2, x, atol=0, rtol=0)
+    torch.testing.assert_close(x2, ref_x, atol=3e-2, rtol=3e-2)
     torch.testing.assert_close(look.pose, pose, atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(look.fields, model.slot_fields(), atol=1e-6, rtol=1e-5)
+    x3, look3 = model.embed_fused(images, fused_tokenizer=False)
+    torch.testing.assert_close(x3, x, atol=0, rtol=0)
+
+
+def test_tokenizer_gemm_matches_float64_and_unfused(model, cuda_device):
+    """The fused tokenizer GEMM (one tcgen05 kernel, softmaxes from the fp32
+    accumulators) against the float64 computation on the same bf16 patches and
+    weights, and against the cuBLAS GEMM + embed_post path (bf16 response)
+    within that path's rounding.  5 images = 975 rows: a partial last row tile;
+    K = 1680: a partial last K slab."""
+    batch, n = 5, model.num_patches
+    images = torch.randn(batch, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(21))
+    patches = ops.gather_patches(images, model.pixel_index, model.pixel_weight)
+    wt, _ = model._tokenizer_weights(cuda_device)
+    params = dict(token_null=model.patch_embed.null_score.detach().float().contiguous(),
+                  direction_coef=model.direction_coefficients.contiguous(),
+                  output_bias=model.patch_embed.output_bias.detach().float().contiguous(),
+                  cls=model.cls_token.detach().float().reshape(-1).contiguous(),
+                  pos_embed=model.pos_embed.detach().float().reshape(n + 1, EMBED_DIM).contiguous(),
+                  look_null=model.look_bank.null_score.detach().float().contiguous())
+    x = torch.full((batch, n + 1, EMBED_DIM), float("nan"), device=cuda_device)
+    pose = torch.full((batch, n, 36, 12), float("nan"), device=cuda_device)
+    ops.tokenizer_gemm(patches, wt, batch=batch, patches_per_image=n, bases=96, directions=6, look_heads=36,
+                       look_poses=12, x=x, look_pose=pose, **params)
+    resp = patches.double() @ wt.double().T
+    tok = resp[:, :576].reshape(batch, n, 96, 6)
+    tnull = params["token_null"].double()[None, None, :, None].expand(batch, n, 96, 1)
+    w = torch.cat((tok, tnull), -1).softmax(-1)[..., :-1]
+    tokens = torch.einsum("bnpd,dc->bnpc", w, params["direction_coef"].double()).reshape(batch, n, EMBED_DIM)
+    tokens = tokens + params["output_bias"].double()
+    ref_x = torch.cat((params["cls"].double().expand(batch, 1, -1), tokens), dim=1) + params["pos_embed"].double()
+    look = resp[:, 576:].reshape(batch, n, 36, 12)
+    lnull = params["look_null"].double()[None, None, :, None].expand(batch, n, 36, 1)
+    ref_pose = torch.cat((look, lnull), -1).softmax(-1)[..., :-1]
+    assert (x.double() - ref_x).abs().max().item() <= 1e-4
+    assert (pose.double() - ref_pose).abs().max().item() <= 1e-5
+    x_old, look_old = model.embed_fused(images, fused_tokenizer=False)
+    torch.testing.assert_close(x, x_old, atol=2e-2, rtol=0)
+    torch.testing.assert_close(pose, look_old.pose, atol=1e-2, rtol=0)
+
+
+def test_tokenizer_gemm_rejects_what_it_cannot_take(model, cuda_device):
+    n = model.num_patches
+    patches = torch.zeros(2 * n, 1680, dtype=torch.bfloat16, device=cuda_device)
+    wt, _ = model._tokenizer_weights(cuda_device)
+    z = lambda *s: torch.zeros(*s, device=cuda_device)  # noqa: E731
+    kw = dict(token_null=z(96), direction_coef=z(6, 2), output_bias=z(192), cls=z(192), pos_embed=z(n + 1, 192),
+              look_null=z(36), x=z(2, n + 1, 192), look_pose=z(2, n, 36, 12))
+    with pytest.raises(ValueError):
+        ops.tokenizer_gemm(patches, wt[:-1], batch=2, patches_per_image=n, bases=96, directions=6, look_heads=36,
+                           look_poses=12, **kw)
+    with pytest.raises(RuntimeError):  # 10 bases: not a multiple of the kernel's 24-base tile
+        ops.tokenizer_gemm(patches, wt[: 60 + 432], batch=2, patches_per_image=n, bases=10, directions=6,
+                           look_heads=36, look_poses=12, **{**kw, "x": z(2, n + 1, 20), "output_bias": z(20),
+                                                            "cls": z(20), "pos_embed": z(n + 1, 20),
+                                                            "token_null": z(10)})
 
 
 def test_look_pose_trunk_matches_per_slot_values(model, cuda_device):
