@@ -20,8 +20,12 @@
 // instruction) into one of two TMEM accumulators; two groups of four
 // epilogue warps (2-5, 6-9: warp w reads TMEM lanes 32 (w % 4) .. + 31) take
 // alternate tiles and run the epilogue from TMEM, one row per thread, while
-// the next tile accumulates in the other buffer.  Every wait is bounded
-// (sm100_ptx.cuh).
+// the next tile accumulates in the other buffer.  The tokenizer instead takes
+// 256-row tiles as two 128-row accumulators that share each weight slab
+// (half the weight's trips through shared memory per row); its 2 x 144 TMEM
+// columns leave no room for a second buffer, so both epilogue groups drain
+// one tile together, each its own 128 rows, and hand the accumulator back as
+// soon as it sits in registers.  Every wait is bounded (sm100_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cstdint>
@@ -43,9 +47,15 @@ __host__ __device__ constexpr int epi_groups_per_tile() { return EPI == 1 || EPI
 template <int EPI>
 __host__ __device__ constexpr int gemm_threads() { return 64 + 2 * epi_groups_per_tile<EPI>() * 128; }
 constexpr int kEpiGelu = 0, kEpiResidualLN = 1, kEpiBias = 2, kEpiTokenizer = 3;
-// Per epilogue warp, in 32-bit words: GELU two 32 x 32 bf16 blocks; LN two 32 x 32 fp32 residual chunks.
+// 128-row sub-tiles per tile (sharing the weight slab) and TMEM accumulator buffers.
 template <int EPI>
-__host__ __device__ constexpr int stage_words() { return EPI == 3 ? 0 : (EPI == 1 ? 2048 : 1024); }
+__host__ __device__ constexpr int m_subtiles() { return EPI == 3 ? 2 : 1; }
+template <int EPI>
+__host__ __device__ constexpr int acc_buffers() { return EPI == 3 ? 1 : 2; }
+// Per epilogue warp, in 32-bit words: GELU two 32 x 32 bf16 blocks; LN two 32 x 32 fp32 residual chunks;
+// tokenizer 32 rows x 52 fp32.
+template <int EPI>
+__host__ __device__ constexpr int stage_words() { return EPI == 3 ? 32 * 52 : (EPI == 1 ? 2048 : 1024); }
 constexpr int kMaxGeluN = 4096;         // GELU bias columns kept in shared memory
 constexpr uint32_t kBarrierBytes = 256;  // room reserved for the barrier block
 
@@ -53,7 +63,7 @@ struct GemmArgs {
   int64_t M;
   int32_t N, K;
   int32_t n_tiles_n;   // N / NT
-  int64_t tiles;       // ceil(M / 128) * n_tiles_n
+  int64_t tiles;       // ceil(M / (128 * row sub-tiles)) * n_tiles_n
   const float* bias;   // (N)
   __nv_bfloat16* out;  // GELU: (M, N) bf16, row stride out_stride
   int64_t out_stride;
@@ -397,89 +407,144 @@ __device__ __forceinline__ void epilogue_residual_ln(uint32_t acc, const float* 
 
 // Tokenizer epilogue of one warp (32 rows = lanes) on a 144-column tile: 24
 // tokenizer bases x 6 directions, or 12 Look heads x 12 poses (the weight's
-// Look rows are ordered head by head).  48 columns (8 bases / 4 heads) per
-// step; the accumulator is released once its last columns are loaded.
+// Look rows are ordered head by head).  The thread's whole 144-column row
+// is loaded into registers and the accumulator released before any math, so
+// that the next tile's MMAs (single TMEM buffer) wait only for the loads.
 //   base p: s_d = C[6p + d], null n_p: e_d = exp(s_d - m), m = max(n_p, s),
 //     x[2p + c] = sum_d e_d coef[d, c] / (exp(n_p - m) + sum_d e_d) + bias + pos
 //   head h: pose[pp] = exp(s_pp - m) / (exp(n_h - m) + sum exp(s - m))
 // (the null state's share is dropped, as in the reference).
+// A tile's outputs are 48 floats per row (a token tile's 24 bases x 2; a
+// Look step of 4 heads x 12), contiguous in x / the Look pose, with rows far
+// apart.  They pass through a per-warp staging block (32 rows x 52 floats:
+// the padding makes the row-per-thread float4 accesses conflict free), so
+// that global memory sees whole 16-byte chunks of consecutive rows, 12 per
+// row, from all 32 lanes at once - not 32 scattered rows per instruction.
+// The position-embedding rows of a token tile come in the same way.
 constexpr int kTokDirs = 6, kLookPoses = 12, kTokTileN = 144;
+constexpr int kTokChunk = 48, kTokStageStride = 52;  // floats per row: used, allocated
+
+// Copies the warp's 32 staged rows to / from global memory: row r at
+// base + offset of lane r (each lane passes its own row's offset), 48 floats
+// each, as 12 float4 per row spread over the lanes; rows with keep == false
+// (of lane r) are skipped.
+template <bool kToGlobal>
+__device__ __forceinline__ void tok_rows_copy(float* stage, float* base, int64_t offset, bool keep, int lane) {
+#pragma unroll
+  for (int j = 0; j < 32 * (kTokChunk / 4) / 32; ++j) {
+    const int idx = lane + 32 * j, rr = idx / (kTokChunk / 4), ch = idx - rr * (kTokChunk / 4);
+    const int64_t off = __shfl_sync(0xffffffffu, offset, rr);
+    const bool k = __shfl_sync(0xffffffffu, keep, rr);
+    float4* sm = reinterpret_cast<float4*>(stage + rr * kTokStageStride) + ch;
+    if (kToGlobal) {
+      if (k) reinterpret_cast<float4*>(base + off)[ch] = *sm;
+    } else {
+      *sm = __ldg(reinterpret_cast<const float4*>(base + off) + ch);
+    }
+  }
+}
+
+// A token tile's position-embedding rows into the staging block, fetched
+// while the tile still accumulates (the accumulator registers are not live yet).
+__device__ __forceinline__ void tokenizer_stage_pos(int64_t tile_n, int64_t m, const GemmArgs& g, int lane,
+                                                    float* stage) {
+  if (tile_n >= g.tok_tiles) return;
+  const int64_t n = m < g.M ? m % g.patches : 0;
+  const int dim = 2 * static_cast<int>(g.tok_tiles) * (kTokTileN / kTokDirs);
+  tok_rows_copy<false>(stage, const_cast<float*>(g.pos_embed), (n + 1) * dim + tile_n * 2 * (kTokTileN / kTokDirs),
+                       true, lane);
+  __syncwarp();
+}
+
 __device__ __forceinline__ void epilogue_tokenizer(uint32_t acc, int64_t tile_n, int64_t m, const GemmArgs& g,
-                                                   int lane, uint64_t* acc_empty) {
+                                                   int lane, float* stage, uint64_t* acc_empty) {
+  uint32_t r[kTokTileN / 16][16];
+#pragma unroll
+  for (int c = 0; c < kTokTileN / 16; ++c) tmem_ld16(acc + 16 * c, r[c]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int c = 0; c < kTokTileN / 16; ++c) reg_fence16(r[c]);
+  release_acc(acc_empty, lane);
   const bool valid = m < g.M;
   const int64_t img = valid ? m / g.patches : 0, n = valid ? m - img * g.patches : 0;
-  const bool tok = tile_n < g.tok_tiles;
   const int dim = 2 * static_cast<int>(g.tok_tiles) * (kTokTileN / kTokDirs);  // 2 * bases
-#pragma unroll 1
-  for (int st = 0; st < 3; ++st) {
-    uint32_t r0[16], r1[16], r2[16];
-    tmem_ld16(acc + 48 * st, r0);
-    tmem_ld16(acc + 48 * st + 16, r1);
-    tmem_ld16(acc + 48 * st + 32, r2);
-    tmem_wait_ld();
-    reg_fence16(r0);
-    reg_fence16(r1);
-    reg_fence16(r2);
-    if (st == 2) release_acc(acc_empty, lane);
-    float v[48];
+  float* srow = stage + lane * kTokStageStride;
+  if (tile_n < g.tok_tiles) {
+    const int p0 = static_cast<int>(tile_n) * (kTokTileN / kTokDirs);  // first base of the tile
+    const int c0 = 2 * p0;                                             // its first x column
+    // the staging block holds this tile's position rows (tokenizer_stage_pos)
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      v[e] = __uint_as_float(r0[e]);
-      v[16 + e] = __uint_as_float(r1[e]);
-      v[32 + e] = __uint_as_float(r2[e]);
-    }
-    if (!valid) continue;
-    if (tok) {
-      const int p0 = static_cast<int>(tile_n) * (kTokTileN / kTokDirs) + 8 * st;  // first base of the step
-      float* xrow = g.x + (img * (g.patches + 1) + n + 1) * dim;
-      const float* pos = g.pos_embed + (n + 1) * dim;
+    for (int i2 = 0; i2 < kTokTileN / kTokDirs; i2 += 2) {
+      float out[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int p = p0 + i;
+      for (int u = 0; u < 2; ++u) {
+        const int i = i2 + u, p = p0 + i;
+        float s[kTokDirs];
+#pragma unroll
+        for (int d = 0; d < kTokDirs; ++d) s[d] = __uint_as_float(r[(kTokDirs * i + d) >> 4][(kTokDirs * i + d) & 15]);
         const float nul = __ldg(g.token_null + p);
         float mx = nul;
 #pragma unroll
-        for (int d = 0; d < kTokDirs; ++d) mx = fmaxf(mx, v[kTokDirs * i + d]);
+        for (int d = 0; d < kTokDirs; ++d) mx = fmaxf(mx, s[d]);
         float sum = __expf(nul - mx), tx = 0.f, ty = 0.f;
 #pragma unroll
         for (int d = 0; d < kTokDirs; ++d) {
-          const float e = __expf(v[kTokDirs * i + d] - mx);
+          const float e = __expf(s[d] - mx);
           sum += e;
           tx = fmaf(e, __ldg(g.direction_coef + 2 * d), tx);
           ty = fmaf(e, __ldg(g.direction_coef + 2 * d + 1), ty);
         }
         const float inv = 1.f / sum;
-        *reinterpret_cast<float2*>(xrow + 2 * p) =
-            make_float2(fmaf(tx, inv, __ldg(g.output_bias + 2 * p) + __ldg(pos + 2 * p)),
-                        fmaf(ty, inv, __ldg(g.output_bias + 2 * p + 1) + __ldg(pos + 2 * p + 1)));
+        out[2 * u] = tx * inv;
+        out[2 * u + 1] = ty * inv;
       }
-      if (n == 0) {  // this image's CLS row, the same 16 columns
-        float* crow = g.x + img * (g.patches + 1) * dim;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) crow[2 * p0 + c] = __ldg(g.cls + 2 * p0 + c) + __ldg(g.pos_embed + 2 * p0 + c);
+      float4* cell = reinterpret_cast<float4*>(srow + 2 * i2);
+      const float4 pos = *cell, bias = __ldg(reinterpret_cast<const float4*>(g.output_bias + c0 + 2 * i2));
+      *cell = make_float4(out[0] + (bias.x + pos.x), out[1] + (bias.y + pos.y), out[2] + (bias.z + pos.z),
+                          out[3] + (bias.w + pos.w));
+    }
+    __syncwarp();
+    tok_rows_copy<true>(stage, g.x, (img * (g.patches + 1) + n + 1) * dim + c0, valid, lane);
+    if (valid && n == 0) {  // this image's CLS row, the same 48 columns
+      float4* crow = reinterpret_cast<float4*>(g.x + img * (g.patches + 1) * dim + c0);
+#pragma unroll 4
+      for (int c = 0; c < kTokChunk / 4; ++c) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(g.cls + c0) + c);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(g.pos_embed + c0) + c);
+        crow[c] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
       }
-    } else {
-      const int h0 = static_cast<int>(tile_n - g.tok_tiles) * (kTokTileN / kLookPoses) + 4 * st;
+    }
+    __syncwarp();
+  } else {
+    const int h0 = static_cast<int>(tile_n - g.tok_tiles) * (kTokTileN / kLookPoses);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int hh = h0 + i;
+    for (int st = 0; st < kTokTileN / kTokChunk; ++st) {
+#pragma unroll
+      for (int i = 0; i < kTokChunk / kLookPoses; ++i) {
+        const int col = kTokChunk * st + kLookPoses * i, hh = h0 + col / kLookPoses;
+        float e[kLookPoses];
+#pragma unroll
+        for (int pp = 0; pp < kLookPoses; ++pp) e[pp] = __uint_as_float(r[(col + pp) >> 4][(col + pp) & 15]);
         const float nul = __ldg(g.look_null + hh);
         float mx = nul;
 #pragma unroll
-        for (int pp = 0; pp < kLookPoses; ++pp) mx = fmaxf(mx, v[kLookPoses * i + pp]);
-        float e[kLookPoses];
+        for (int pp = 0; pp < kLookPoses; ++pp) mx = fmaxf(mx, e[pp]);
         float sum = __expf(nul - mx);
 #pragma unroll
         for (int pp = 0; pp < kLookPoses; ++pp) {
-          e[pp] = __expf(v[kLookPoses * i + pp] - mx);
+          e[pp] = __expf(e[pp] - mx);
           sum += e[pp];
         }
         const float inv = 1.f / sum;
-        float4* dst = reinterpret_cast<float4*>(g.look_pose + (m * g.look_heads + hh) * kLookPoses);
+        float4* cell = reinterpret_cast<float4*>(srow + kLookPoses * i);
 #pragma unroll
         for (int c = 0; c < kLookPoses / 4; ++c)
-          dst[c] = make_float4(e[4 * c] * inv, e[4 * c + 1] * inv, e[4 * c + 2] * inv, e[4 * c + 3] * inv);
+          cell[c] = make_float4(e[4 * c] * inv, e[4 * c + 1] * inv, e[4 * c + 2] * inv, e[4 * c + 3] * inv);
       }
+      __syncwarp();
+      tok_rows_copy<true>(stage, g.look_pose, (m * g.look_heads + h0 + st * (kTokChunk / kLookPoses)) * kLookPoses,
+                          valid, lane);
+      __syncwarp();
     }
   }
 }
@@ -488,9 +553,12 @@ template <int NT, int STAGES, int EPI>
 __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const GemmArgs g) {
+  constexpr int kMSub = m_subtiles<EPI>(), kBufs = acc_buffers<EPI>();
+  constexpr int64_t kTileM = kMSub * kGBM;
   constexpr uint32_t kBSlab = NT * kGBK * 2;
-  constexpr uint32_t kStage = kASlab + kBSlab;
-  constexpr uint32_t kTmemCols = 2 * NT <= 256 ? 256 : 512;
+  constexpr uint32_t kStage = kMSub * kASlab + kBSlab;  // A sub-tiles, then the weight slab
+  constexpr uint32_t kTmemCols = kBufs * kMSub * NT <= 256 ? 256 : 512;
+  static_assert(kBufs * kMSub * NT <= 512, "TMEM columns");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   GemmBarriers<STAGES>* bars = reinterpret_cast<GemmBarriers<STAGES>*>(smem + STAGES * kStage);
@@ -504,7 +572,7 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
-      mbar_init(&bars->acc_empty[b], 4 * epi_groups_per_tile<EPI>());
+      mbar_init(&bars->acc_empty[b], 4 * epi_groups_per_tile<EPI>() * kMSub);
     }
     mbar_init(&bars->drain, 1);
     mbar_init(&bars->params, 1);
@@ -529,8 +597,11 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       uint32_t loads = 0, stage = 0, phase = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-        const int32_t m0 = static_cast<int32_t>((t / g.n_tiles_n) * kGBM);
+        const int32_t m0 = static_cast<int32_t>((t / g.n_tiles_n) * kTileM);
         const int32_t n0 = static_cast<int32_t>((t % g.n_tiles_n) * NT);
+        // a second row sub-tile wholly past M is neither loaded nor multiplied
+        const bool sub1 = kMSub == 2 && m0 + kGBM < g.M;
+        const uint32_t bytes = kStage - (kMSub == 2 && !sub1 ? kASlab : 0u);
         for (int ks = 0; ks < n_slabs; ++ks) {
           if (loads >= STAGES &&
               !mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, g.status, kDevTimeoutProducer)) {
@@ -538,9 +609,10 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
             break;
           }
           uint8_t* dst = smem + stage * kStage;
-          mbar_arrive_expect_tx(&bars->full[stage], kStage);
+          mbar_arrive_expect_tx(&bars->full[stage], bytes);
           tma_load_2d(dst, &tm_a, &bars->full[stage], ks * kGBK, m0);
-          tma_load_2d(dst + kASlab, &tm_b, &bars->full[stage], ks * kGBK, n0);
+          if (sub1) tma_load_2d(dst + kASlab, &tm_a, &bars->full[stage], ks * kGBK, m0 + kGBM);
+          tma_load_2d(dst + kMSub * kASlab, &tm_b, &bars->full[stage], ks * kGBK, n0);
           ++loads;
           if (++stage == STAGES) {
             stage = 0;
@@ -560,16 +632,18 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(true, false, kGBM, NT);
       const uint64_t a_desc = smem_desc_sw128(smem_u32(smem), 16, 1024);
-      const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + kASlab), 16, 1024);
+      const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + kMSub * kASlab), 16, 1024);
       uint32_t stage = 0, phase = 0, lt = 0;
       bool ok = true, issued = false;
       for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++lt) {
-        const uint32_t buf = lt & 1;
-        if (lt >= 2 &&
-            !mbar_wait(&bars->acc_empty[buf], ((lt - 2) >> 1) & 1, abort_flag, g.status, kDevTimeoutMma)) {
+        const uint32_t buf = lt % kBufs;
+        if (lt >= kBufs &&
+            !mbar_wait(&bars->acc_empty[buf], ((lt - kBufs) / kBufs) & 1, abort_flag, g.status, kDevTimeoutMma)) {
           ok = false;
           break;
         }
+        const bool sub1 = kMSub == 2 && (t / g.n_tiles_n) * kTileM + kGBM < g.M;
+        const uint32_t d_tmem = tmem + buf * kMSub * NT;
         tc_fence_after();
         for (int ks = 0; ks < n_slabs; ++ks) {
           if (!mbar_wait(&bars->full[stage], phase, abort_flag, g.status, kDevTimeoutMma)) {
@@ -578,9 +652,13 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
           }
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < kGBK / 16; ++kk)
-            mma_ss(tmem + buf * NT, a_desc + ((stage * kStage + kk * 32) >> 4),
-                   b_desc + ((stage * kStage + kk * 32) >> 4), idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kGBK / 16; ++kk) {
+            const uint64_t b_k = b_desc + ((stage * kStage + kk * 32) >> 4);
+            mma_ss(d_tmem, a_desc + ((stage * kStage + kk * 32) >> 4), b_k, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+            if (sub1)
+              mma_ss(d_tmem + NT, a_desc + ((stage * kStage + kASlab + kk * 32) >> 4), b_k, idesc,
+                     (ks > 0 || kk > 0) ? 1u : 0u);
+          }
           mma_commit(&bars->empty[stage]);
           issued = true;
           if (++stage == STAGES) {
@@ -627,19 +705,26 @@ gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     uint32_t* stage = reinterpret_cast<uint32_t*>(smem + STAGES * kStage + kBarrierBytes) + (warp - 2) * stage_words<EPI>();
     uint32_t lt = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++lt) {
-      if ((lt & 1) != e) continue;
-      const int32_t n0 = static_cast<int32_t>((t % g.n_tiles_n) * NT);
-      const uint32_t acc = lane_base + e * NT + col0;
-      const int64_t wrow0 = (t / g.n_tiles_n) * kGBM + (warp & 3) * 32;  // first row of this warp
-      if (EPI == kEpiTokenizer) {
-        if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
+    if (EPI == kEpiTokenizer) {
+      // Both groups take every tile: group grp drains row sub-tile grp.
+      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++lt) {
+        const int64_t row = (t / g.n_tiles_n) * kTileM + grp * kGBM + (warp & 3) * 32 + lane;
+        tokenizer_stage_pos(t % g.n_tiles_n, row, g, lane, reinterpret_cast<float*>(stage));
+        if (!mbar_wait(&bars->acc_full[0], lt & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        epilogue_tokenizer(acc, t % g.n_tiles_n, wrow0 + lane, g, lane, &bars->acc_empty[e]);
-      } else if (EPI != kEpiResidualLN) {
+        epilogue_tokenizer(lane_base + grp * NT, t % g.n_tiles_n, row, g, lane, reinterpret_cast<float*>(stage),
+                           &bars->acc_empty[0]);
+      }
+    }
+    for (int64_t t = blockIdx.x; EPI != kEpiTokenizer && t < g.tiles && ok; t += gridDim.x, ++lt) {
+      if ((lt & 1) != e) continue;
+      const int32_t n0 = static_cast<int32_t>((t % g.n_tiles_n) * NT);
+      const uint32_t acc = lane_base + e * NT + col0;
+      const int64_t wrow0 = (t / g.n_tiles_n) * kGBM + (warp & 3) * 32;  // first row of this warp
+      if (EPI != kEpiResidualLN) {
         if (!mbar_wait(&bars->acc_full[e], (lt >> 1) & 1, abort_flag, g.status, kDevTimeoutSoftmax)) {
           ok = false;
           break;
@@ -717,7 +802,8 @@ intp_status launch_gemm(const void* a, int64_t a_stride, const void* w, GemmArgs
   if (!make_map_2d(&ma, a, g.M, g.K, a_stride, kGBM) || !make_map_2d(&mb, w, g.N, g.K, g.K, NT))
     return INTP_ERR_LAYOUT;
   g.n_tiles_n = g.N / NT;
-  g.tiles = ((g.M + kGBM - 1) / kGBM) * g.n_tiles_n;
+  constexpr int64_t kTileM = m_subtiles<EPI>() * kGBM;
+  g.tiles = ((g.M + kTileM - 1) / kTileM) * g.n_tiles_n;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -725,7 +811,7 @@ intp_status launch_gemm(const void* a, int64_t a_stride, const void* w, GemmArgs
   auto kernel = gemm_epilogue_kernel<NT, STAGES, EPI>;
   static_assert(sizeof(GemmBarriers<STAGES>) <= kBarrierBytes, "barrier block");
   const size_t params = EPI == kEpiTokenizer ? 0 : (EPI != kEpiResidualLN ? static_cast<size_t>(g.N) : 3 * NT);
-  const size_t smem = 1024 + STAGES * (kASlab + NT * kGBK * 2) + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4 + params * 4;
+  const size_t smem = 1024 + STAGES * (m_subtiles<EPI>() * kASlab + NT * kGBK * 2) + kBarrierBytes + 8 * epi_groups_per_tile<EPI>() * stage_words<EPI>() * 4 + params * 4;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return INTP_ERR_LAUNCH;
@@ -830,7 +916,9 @@ extern "C" INTP_API intp_status svit_tokenizer_gemm(const svit_embed_args* args,
   if (a.values != nullptr || !a.look_pose || !a.x || !a.token_null || !a.direction_coef || !a.output_bias || !a.cls ||
       !a.pos_embed || !a.look_null)
     return INTP_ERR_ARGUMENT;
-  if (features % 8 || patches_stride < features || !aligned16(a.look_pose)) return INTP_ERR_LAYOUT;
+  if (features % 8 || patches_stride < features || !aligned16(a.look_pose) || !aligned16(a.x) ||
+      !aligned16(a.pos_embed) || !aligned16(a.cls) || !aligned16(a.output_bias))
+    return INTP_ERR_LAYOUT;
   if (!device_is_sm100()) return INTP_ERR_ARCH;
   GemmArgs g{};
   g.M = a.batch * a.patches;
@@ -848,6 +936,6 @@ extern "C" INTP_API intp_status svit_tokenizer_gemm(const svit_embed_args* args,
   g.look_null = a.look_null;
   g.look_pose = a.look_pose;
   g.look_heads = a.look_heads;
-  return launch_gemm<kTokTileN, 4, kEpiTokenizer>(patches, patches_stride, weight, g,
+  return launch_gemm<kTokTileN, 3, kEpiTokenizer>(patches, patches_stride, weight, g,
                                                    static_cast<cudaStream_t>(stream));
 }

@@ -106,13 +106,17 @@ def test_embed_fused_matches_unfused(model, cuda_device):
     torch.testing.assert_close(x3, x, atol=0, rtol=0)
 
 
-def test_tokenizer_gemm_matches_float64_and_unfused(model, cuda_device):
+@pytest.mark.parametrize("batch", [3, 5, 64])
+def test_tokenizer_gemm_matches_float64_and_unfused(model, cuda_device, batch):
     """The fused tokenizer GEMM (one tcgen05 kernel, softmaxes from the fp32
     accumulators) against the float64 computation on the same bf16 patches and
     weights, and against the cuBLAS GEMM + embed_post path (bf16 response)
-    within that path's rounding.  5 images = 975 rows: a partial last row tile;
-    K = 1680: a partial last K slab."""
-    batch, n = 5, model.num_patches
+    within that path's rounding.  256-row tiles of two 128-row halves: 3 images
+    = 585 rows (the last tile's second half wholly past the end), 5 images =
+    975 rows (a partial second half), 64 images = 12480 rows (343 tiles: CTAs
+    take up to three tiles through the single accumulator); K = 1680: a
+    partial last K slab."""
+    n = model.num_patches
     images = torch.randn(batch, 3, 224, 224, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(21))
     patches = ops.gather_patches(images, model.pixel_index, model.pixel_weight)
     wt, _ = model._tokenizer_weights(cuda_device)
