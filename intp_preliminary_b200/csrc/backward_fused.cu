@@ -399,6 +399,18 @@ sla_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const uint32_t xcol = lane_base + st * 128 + 32 * half;
       load_scores<32>(xcol, xcol + 64, sr, dr);
       const int32_t k0 = j * kCols + 32 * half;
+      // Slot sums take only pairs with a Look slot (byte < ns); "no bias" and
+      // "past the end" pairs are the large majority away from the query's
+      // neighbourhood, and their sums are discarded.  A warp whose 32 rows have
+      // no slotted pair in this tile skips the read-add-writes altogether.
+      bool slotted = false;
+      if (use_bias) {
+        const uint32_t lim = 0x01010101u * static_cast<uint32_t>(a.n_slots);
+        const uint32_t m = __vcmpltu4(cur[0].x, lim) | __vcmpltu4(cur[0].y, lim) | __vcmpltu4(cur[0].z, lim) |
+                           __vcmpltu4(cur[0].w, lim) | __vcmpltu4(cur[1].x, lim) | __vcmpltu4(cur[1].y, lim) |
+                           __vcmpltu4(cur[1].z, lim) | __vcmpltu4(cur[1].w, lim);
+        slotted = __any_sync(0xffffffffu, m != 0u);
+      }
       uint32_t dw[16];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -420,8 +432,11 @@ sla_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           }
           // each cell of this warpgroup's array has one writer (this thread): a plain
           // read-add-write (measured faster than red.shared.add.f32 here)
+          if (slotted) {
 #pragma unroll
-          for (int e2 = 0; e2 < 8; ++e2) drow[sl[e2] * kRows] += g[e2];  // [ns], [ns + 1]: sinks
+            for (int e2 = 0; e2 < 8; ++e2)
+              if (sl[e2] < static_cast<uint32_t>(a.n_slots)) drow[sl[e2] * kRows] += g[e2];
+          }
         } else {
 #pragma unroll
           for (int e2 = 0; e2 < 8; ++e2) {
