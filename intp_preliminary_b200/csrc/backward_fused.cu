@@ -53,8 +53,12 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColAcc0 = 256, kColAcc1 = 320;  // dQ | dK, dV
 constexpr uint32_t kMinSmem = 120 * 1024;           // one CTA per SM (it holds all 512 TMEM columns)
 
+constexpr int kStageBufs = 3;                 // dkdv: stage blocks (tile t in block t % 3)
+
 struct alignas(8) FusedBars {
   uint64_t fixed_full;                        // the CTA's resident operand pair
+  uint64_t stage_full[kStageBufs];            // dkdv: a stage block's copies landed (every row thread)
+  uint64_t stage_free[kStageBufs];            // dkdv: every row warp has read a stage block
   uint64_t ring_full[kStages], ring_empty[kStages];
   uint64_t s_full[2], ready[2], buf_free[2];
   uint64_t acc_full, drain;
@@ -492,20 +496,22 @@ sla_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 }
 
 // ============================================================================ dK, dV
-// Stage block of one 64-query tile: table[64][table_w] (Look values in the
-// log2 domain minus the query's lse * log2(e); table_w = round_up(ns + 2, 4);
-// column ns = -lse * log2(e) ("no bias"), column ns + 1 = -inf (query past the
-// end), written once per CTA), then lse * log2(e) [64] (used without Look
-// bias), then delta [64].  Thread t copies query row t / 8 (its 16-byte slot
-// groups t % 8 + 8m, or its slots t % 8 + 8m one by one when the rows are not
-// 16-byte aligned) and, for t < 128, one lse / delta value, with cp.async
-// straight into shared memory two tiles ahead; the row's lse travels in a
-// register.  Once the copy has landed the same thread rescales its entries.
-// Rows and queries outside 1..N-1 / 0..N-1 are zero-filled (the slot table
-// sends those pairs to the constant columns).
+// Stage block of one 64-query tile: table[64][table_w] (the queries' Look
+// values as stored; table_w = round_up(ns + 2, 4); column ns = 0 ("no bias")
+// and column ns + 1 = -inf (query past the end), both written once per CTA),
+// then lse [64], then delta [64].  Thread t copies query row t / 8 (its
+// 16-byte slot groups t % 8 + 8m, or its slots t % 8 + 8m one by one when the
+// rows are not 16-byte aligned) and, for t < 128, one lse / delta value, with
+// cp.async straight into shared memory two tiles ahead, and hands the copies'
+// completion to the block's stage_full barrier (cp.async.mbarrier.arrive).
+// The log2(e) scaling and the query's lse are applied where the values are
+// used (t = S scale log2 e + (v - lse) log2 e), so no thread rewrites a block
+// and the row threads never meet at a CTA-wide barrier: a block is reused
+// once every row warp has arrived on its stage_free barrier.  Rows and
+// queries outside 1..N-1 / 0..N-1 are zero-filled (the slot table sends those
+// pairs to the constant columns).
 constexpr int kKvThreads = kKvRowThreads + 32;
 constexpr int kKvMmaWarp = kKvRowThreads / 32;
-constexpr int kStageBufs = 3;
 constexpr int kStageLanes = kKvRowThreads / kCols;  // threads per query row: 8
 constexpr int kMaxStageVec = (kMaxLookSlots / 4 + kStageLanes - 1) / kStageLanes;
 constexpr int kMaxStageScalar = (kMaxLookSlots + kStageLanes - 1) / kStageLanes;
@@ -518,16 +524,16 @@ __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool pre
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(pred ? 4 : 0)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Arrive on `bar` once this thread's earlier cp.async copies have landed (the
+// barrier's count includes this arrival: .noinc).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Issues this thread's copies of tile (q0..q0+63)'s stage block; returns its
-// query row's lse * log2(e) (0 past the end).
+// Issues this thread's copies of tile (q0..q0+63)'s stage block.
 template <class A>
-__device__ __forceinline__ float stage_issue(float* blk, const A& a, int tid, int32_t q0, int64_t b, int64_t h) {
+__device__ __forceinline__ void stage_issue(float* blk, const A& a, int tid, int32_t q0, int64_t b, int64_t h) {
   const SlaParams& p = a.p;
   const int32_t N = static_cast<int32_t>(p.seq);
   const int ns = a.n_slots, tw = a.table_w;
@@ -559,38 +565,6 @@ __device__ __forceinline__ float stage_issue(float* blk, const A& a, int tid, in
     const float* base = tid < kCols ? p.lse : a.delta;
     cp_async4(blk + kCols * tw + tid, base + bh_off + (tq < N ? tq : 0), tq < N);
   }
-  return tok < N ? __ldg(p.lse + bh_off + tok) * kLog2eF : 0.f;
-}
-
-// After this thread's copies landed: its table entries to log2(e) v - lse2,
-// the row's "no bias" entry, and (t < 64) one lse to the log2 domain.
-__device__ __forceinline__ void stage_scale(float* blk, int tid, int tw, int ns, bool vec4, float lse2) {
-  const int q = tid / kStageLanes, c = tid % kStageLanes;
-  float* row = blk + q * tw;
-  if (ns > 0) {
-    if (vec4) {
-#pragma unroll
-      for (int m = 0; m < kMaxStageVec; ++m) {
-        const int g = c + kStageLanes * m;
-        if (g < ns / 4) {
-          float4 v = *reinterpret_cast<float4*>(row + 4 * g);
-          v.x = fmaf(v.x, kLog2eF, -lse2);
-          v.y = fmaf(v.y, kLog2eF, -lse2);
-          v.z = fmaf(v.z, kLog2eF, -lse2);
-          v.w = fmaf(v.w, kLog2eF, -lse2);
-          *reinterpret_cast<float4*>(row + 4 * g) = v;
-        }
-      }
-    } else {
-#pragma unroll 4
-      for (int m = 0; m < kMaxStageScalar; ++m) {
-        const int sl = c + kStageLanes * m;
-        if (sl < ns) row[sl] = fmaf(row[sl], kLog2eF, -lse2);
-      }
-    }
-    if (c == 0) row[ns] = -lse2;
-  }
-  if (tid < kCols) blk[kCols * tw + tid] *= kLog2eF;
 }
 
 template <bool BF16>
@@ -618,7 +592,13 @@ sla_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   const int tw = a.table_w;
   const int stage_n = kCols * tw + 2 * kCols;
 
-  if (threadIdx.x == 0) init_bars(bars, kKvRowThreads / 32);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStageBufs; ++s) {
+      mbar_init(&bars->stage_full[s], kKvRowThreads);
+      mbar_init(&bars->stage_free[s], kKvRowThreads / 32);
+    }
+    init_bars(bars, kKvRowThreads / 32);
+  }
   if (warp == kKvMmaWarp) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
@@ -640,88 +620,95 @@ sla_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float scale_log2 = p.scale * kLog2eF;
     const int n_t = a.n_col_tiles;
-    // the -inf column of every block, then tiles 0 and 1 in flight
-    if (use_bias && tid < kStageBufs * kCols) stage_s[(tid / kCols) * stage_n + (tid % kCols) * tw + a.n_slots + 1] = -INFINITY;
-    float lse_a = stage_issue(stage_s, a, tid, 0, b, h);
-    cp_async_commit();
-    float lse_b = n_t > 1 ? stage_issue(stage_s + stage_n, a, tid, kCols, b, h) : 0.f;
-    cp_async_commit();
-    cp_async_wait<1>();
-    stage_scale(stage_s, tid, tw, a.n_slots, a.pose_vec4 != 0, lse_a);
-    lse_a = lse_b;                            // lse of tile t + 1's row; lse_b: tile t + 2's
+    // the constant columns of every block, then tiles 0 and 1 in flight
+    if (use_bias && tid < kStageBufs * kCols) {
+      float* crow = stage_s + (tid / kCols) * stage_n + (tid % kCols) * tw + a.n_slots;
+      crow[0] = 0.f;
+      crow[1] = -INFINITY;
+    }
     row_sync<kKvRowThreads>();
+    stage_issue(stage_s, a, tid, 0, b, h);
+    cp_async_arrive(&bars->stage_full[0]);
+    if (n_t > 1) {
+      stage_issue(stage_s + stage_n, a, tid, kCols, b, h);
+      cp_async_arrive(&bars->stage_full[1]);
+    }
     const uint8_t* sbase = a.slots_t + int64_t(kt) * n_t * kSlotTileBytes + wg * 2048 + row * 16;
     uint4 cur, nxt;
     if (use_bias) nxt = __ldg(reinterpret_cast<const uint4*>(sbase));
     bool ok = true;
     for (int t = 0; t < n_t; ++t) {
-      const int st = t & 1;
-      const float* blk = stage_s + (t % kStageBufs) * stage_n;
-      // tile t + 2's stage block into the buffer tile t - 1 used
-      if (t + 2 < n_t) lse_b = stage_issue(stage_s + ((t + 2) % kStageBufs) * stage_n, a, tid, (t + 2) * kCols, b, h);
-      cp_async_commit();
+      const int st = t & 1, sb = t % kStageBufs;
+      const float* blk = stage_s + sb * stage_n;
+      // tile t + 2's stage block into the block tile t - 1 used, once every row warp has read it
+      if (t + 2 < n_t) {
+        const int nb = (t + 2) % kStageBufs;
+        if (t >= 1 && !mbar_wait(&bars->stage_free[nb], ((t - 1) / kStageBufs) & 1, abort_flag, p.status,
+                                 kDevTimeoutSoftmax, a.wait_ns)) {
+          ok = false;
+          break;
+        }
+        stage_issue(stage_s + nb * stage_n, a, tid, (t + 2) * kCols, b, h);
+        cp_async_arrive(&bars->stage_full[nb]);
+      }
       if (use_bias) {  // this tile's slot bytes (loaded one tile ahead); the next tile's in flight
         cur = nxt;
         if (t + 1 < n_t) nxt = __ldg(reinterpret_cast<const uint4*>(sbase + int64_t(t + 1) * kSlotTileBytes));
       }
-      if (!mbar_wait(&bars->s_full[st], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) {
-        ok = false;
-      }
-      if (ok) {
-        tc_fence_after();
-        uint32_t sr[16], dr[16];
-        const uint32_t xcol = lane_base + st * 128 + 16 * wg;
-        load_scores<16>(xcol, xcol + 64, sr, dr);
-        const float4* lse4 = reinterpret_cast<const float4*>(blk + kCols * tw + 16 * wg);
-        const float4* dlt4 = lse4 + kCols / 4;
-        const float* tab = blk + 16 * wg * tw;
-        const int32_t qbase = t * kCols + 16 * wg;
-        uint32_t pw[8], dw[8];
-#pragma unroll
-        for (int e4 = 0; e4 < 16; e4 += 4) {
-          const float4 d4 = dlt4[e4 / 4];
-          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-          float tl[4];
-          if (use_bias) {
-            const uint32_t word = (&cur.x)[e4 >> 2];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) tl[u] = tab[(e4 + u) * tw + __byte_perm(word, 0u, 0x4440u | u)];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) tl[u] = fmaf(__uint_as_float(sr[e4 + u]), scale_log2, tl[u]);
-          } else {
-            const float4 l4 = lse4[e4 / 4];
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              tl[u] = qbase + e4 + u < N ? fmaf(__uint_as_float(sr[e4 + u]), scale_log2, -lv[u]) : -INFINITY;
-          }
-          float pr[4], gg[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            pr[u] = fast_exp2(tl[u]);
-            gg[u] = pr[u] * (__uint_as_float(dr[e4 + u]) - dv[u]);
-          }
-          pw[e4 / 2] = pk2<BF16>(pr[0], pr[1]);
-          pw[e4 / 2 + 1] = pk2<BF16>(pr[2], pr[3]);
-          dw[e4 / 2] = pk2<BF16>(gg[0], gg[1]);
-          dw[e4 / 2 + 1] = pk2<BF16>(gg[2], gg[3]);
-        }
-        tmem_st8(xcol, pw);        // P^T over the read score columns
-        tmem_st8(xcol + 64, dw);   // dS^T over the read dP columns
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->ready[st]);
-      }
-      cp_async_wait<1>();  // tile t + 1's block landed (only tile t + 2's group may be pending)
-      if (t + 1 < n_t) stage_scale(stage_s + ((t + 1) % kStageBufs) * stage_n, tid, tw, a.n_slots, a.pose_vec4 != 0, lse_a);
-      lse_a = lse_b;
-      // one decision for all row threads: a lone early exit would strand the others at this barrier
-      if (row_any<kKvRowThreads>(!ok)) {
+      if (!mbar_wait(&bars->s_full[st], (t >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns) ||
+          !mbar_wait(&bars->stage_full[sb], (t / kStageBufs) & 1, abort_flag, p.status, kDevTimeoutSoftmax,
+                     a.wait_ns)) {
         ok = false;
         break;
       }
+      tc_fence_after();
+      uint32_t sr[16], dr[16];
+      const uint32_t xcol = lane_base + st * 128 + 16 * wg;
+      load_scores<16>(xcol, xcol + 64, sr, dr);
+      const float4* lse4 = reinterpret_cast<const float4*>(blk + kCols * tw + 16 * wg);
+      const float4* dlt4 = lse4 + kCols / 4;
+      const float* tab = blk + 16 * wg * tw;
+      const int32_t qbase = t * kCols + 16 * wg;
+      uint32_t pw[8], dw[8];
+#pragma unroll
+      for (int e4 = 0; e4 < 16; e4 += 4) {
+        const float4 d4 = dlt4[e4 / 4], l4 = lse4[e4 / 4];
+        const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+        float tl[4];
+        if (use_bias) {
+          const uint32_t word = (&cur.x)[e4 >> 2];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) tl[u] = tab[(e4 + u) * tw + __byte_perm(word, 0u, 0x4440u | u)];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            tl[u] = fmaf(__uint_as_float(sr[e4 + u]), scale_log2, (tl[u] - lv[u]) * kLog2eF);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            tl[u] = qbase + e4 + u < N ? fmaf(__uint_as_float(sr[e4 + u]), scale_log2, -lv[u] * kLog2eF) : -INFINITY;
+        }
+        float pr[4], gg[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          pr[u] = fast_exp2(tl[u]);
+          gg[u] = pr[u] * (__uint_as_float(dr[e4 + u]) - dv[u]);
+        }
+        pw[e4 / 2] = pk2<BF16>(pr[0], pr[1]);
+        pw[e4 / 2 + 1] = pk2<BF16>(pr[2], pr[3]);
+        dw[e4 / 2] = pk2<BF16>(gg[0], gg[1]);
+        dw[e4 / 2 + 1] = pk2<BF16>(gg[2], gg[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->stage_free[sb]);  // this warp is through with the block
+      tmem_st8(xcol, pw);        // P^T over the read score columns
+      tmem_st8(xcol + 64, dw);   // dS^T over the read dP columns
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ready[st]);
     }
+    cp_async_wait_all();  // no copy of this thread is still in flight past this point
     if (ok && !mbar_wait(&bars->acc_full, 0, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) ok = false;
     tc_fence_after();
     if (ok) {
