@@ -107,6 +107,21 @@ __device__ __forceinline__ bool row_any(bool v) {
   return r != 0;
 }
 
+// A 128-row x 64-column fp32 gradient block staged in shared memory for the
+// epilogue: row r's 16-byte chunk c sits at chunk position c ^ (r & 15), so
+// the row-per-thread float4 writes and the row-major float4 reads of the
+// copy-out are both free of bank conflicts.  The copy-out moves whole
+// consecutive rows, 32 float4 per warp instruction - where row-per-thread
+// stores would touch 32 rows, a part of a sector each, per instruction.
+__device__ __forceinline__ float4* blk_chunk(float* blk, int r, int c) {
+  return reinterpret_cast<float4*>(blk + r * 64) + (c ^ (r & 15));
+}
+// Rows [0, rows) of a staged block to dst (64 floats per row, rows contiguous).
+__device__ __forceinline__ void blk_copy_out(float* blk, float* dst, int rows, int tid, int nthreads) {
+  for (int idx = tid; idx < rows * 16; idx += nthreads)
+    reinterpret_cast<float4*>(dst)[idx] = *blk_chunk(blk, idx >> 4, idx & 15);
+}
+
 // Sum over 8 pairs of 16-bit values.
 template <bool BF16>
 __device__ __forceinline__ float dot8(uint4 x, uint4 y) {
@@ -460,6 +475,8 @@ sla_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
     if (ok && !mbar_wait(&bars->acc_full, 0, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) ok = false;
     tc_fence_after();
+    // dQ through shared memory: the Q / dO tiles are free once the last MMA is done
+    float* dq_blk = reinterpret_cast<float*>(q_s);
     if (ok) {
       uint32_t q0[16], q1[16];
       tmem_ld16(lane_base + kColAcc0 + 32 * half, q0);
@@ -467,23 +484,37 @@ sla_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       tmem_wait_ld();
       reg_fence16(q0);
       reg_fence16(q1);
-      if (valid && a.grad_q != nullptr) {
-        float4* dst = reinterpret_cast<float4*>(a.grad_q + (int64_t(bh) * N + i) * D64 + 32 * half);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          dst[c] = make_float4(__uint_as_float(q0[4 * c]) * p.scale, __uint_as_float(q0[4 * c + 1]) * p.scale,
-                               __uint_as_float(q0[4 * c + 2]) * p.scale, __uint_as_float(q0[4 * c + 3]) * p.scale);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          dst[4 + c] = make_float4(__uint_as_float(q1[4 * c]) * p.scale, __uint_as_float(q1[4 * c + 1]) * p.scale,
-                                   __uint_as_float(q1[4 * c + 2]) * p.scale, __uint_as_float(q1[4 * c + 3]) * p.scale);
+      for (int c = 0; c < 4; ++c) {
+        *blk_chunk(dq_blk, row, 8 * half + c) =
+            make_float4(__uint_as_float(q0[4 * c]) * p.scale, __uint_as_float(q0[4 * c + 1]) * p.scale,
+                        __uint_as_float(q0[4 * c + 2]) * p.scale, __uint_as_float(q0[4 * c + 3]) * p.scale);
+        *blk_chunk(dq_blk, row, 8 * half + 4 + c) =
+            make_float4(__uint_as_float(q1[4 * c]) * p.scale, __uint_as_float(q1[4 * c + 1]) * p.scale,
+                        __uint_as_float(q1[4 * c + 2]) * p.scale, __uint_as_float(q1[4 * c + 3]) * p.scale);
       }
     }
-    if (use_bias) row_sync<kDqRowThreads>();  // both warpgroups' slot sums are in
-    if (ok && use_bias && half == 0 && a.grad_pose != nullptr && valid && i >= 1) {
-      float* dst = a.grad_pose + ((int64_t(b) * (N - 1) + (i - 1)) * H + h) * a.n_slots;
-      const float* other = drow + (a.n_slots + 2) * kRows;
-      for (int s = 0; s < a.n_slots; ++s) dst[s] = drow[s * kRows] + other[s * kRows];
+    row_sync<kDqRowThreads>();  // dQ staged; both warpgroups' slot sums are in
+    const int tile_rows = N - qt * kRows < kRows ? N - qt * kRows : kRows;
+    if (ok && a.grad_q != nullptr)
+      blk_copy_out(dq_blk, a.grad_q + (int64_t(bh) * N + qt * kRows) * D64, tile_rows, threadIdx.x, kDqRowThreads);
+    if (use_bias) {
+      // slot gradient rows [row][slot] (odd row stride: conflict-free per-row writes) in
+      // the Look table's place, then copied out slot-contiguously
+      const int ns = a.n_slots, pst = ns | 1;
+      float* pblk = table_s;
+      if (ok && half == 0) {
+        const float* other = drow + (ns + 2) * kRows;
+        for (int s = 0; s < ns; ++s) pblk[row * pst + s] = drow[s * kRows] + other[s * kRows];
+      }
+      row_sync<kDqRowThreads>();
+      if (ok && a.grad_pose != nullptr) {
+        for (int idx = threadIdx.x; idx < tile_rows * ns; idx += kDqRowThreads) {
+          const int r = idx / ns, sl = idx - r * ns;
+          const int32_t tok = qt * kRows + r;
+          if (tok >= 1) a.grad_pose[((int64_t(b) * (N - 1) + (tok - 1)) * H + h) * ns + sl] = pblk[r * pst + sl];
+        }
+      }
     }
   }
 
@@ -615,8 +646,6 @@ sla_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     const int tid = threadIdx.x;
     const int row = tid & (kRows - 1);
     const int wg = tid >> 7;                  // query columns 16 wg .. 16 wg + 15 of each tile
-    const int32_t key = kt * kRows + row;
-    const bool valid = key < N;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float scale_log2 = p.scale * kLog2eF;
     const int n_t = a.n_col_tiles;
@@ -711,6 +740,9 @@ sla_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     cp_async_wait_all();  // no copy of this thread is still in flight past this point
     if (ok && !mbar_wait(&bars->acc_full, 0, abort_flag, p.status, kDevTimeoutSoftmax, a.wait_ns)) ok = false;
     tc_fence_after();
+    // dK and dV through shared memory: the K / V tiles and the ring are free once the last MMA is done
+    float* dk_blk = reinterpret_cast<float*>(smem);
+    float* dv_blk = dk_blk + kRows * D64;
     if (ok) {
       uint32_t kr[16], vr[16];
       tmem_ld16(lane_base + kColAcc0 + 16 * wg, kr);
@@ -718,24 +750,20 @@ sla_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       tmem_wait_ld();
       reg_fence16(kr);
       reg_fence16(vr);
-      if (valid) {
-        const int64_t off = (int64_t(bh) * N + key) * D64 + 16 * wg;
-        if (a.grad_k != nullptr) {
-          float4* dst = reinterpret_cast<float4*>(a.grad_k + off);
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            dst[c] = make_float4(__uint_as_float(kr[4 * c]) * p.scale, __uint_as_float(kr[4 * c + 1]) * p.scale,
-                                 __uint_as_float(kr[4 * c + 2]) * p.scale, __uint_as_float(kr[4 * c + 3]) * p.scale);
-        }
-        if (a.grad_v != nullptr) {
-          float4* dst = reinterpret_cast<float4*>(a.grad_v + off);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            dst[c] = make_float4(__uint_as_float(vr[4 * c]), __uint_as_float(vr[4 * c + 1]),
-                                 __uint_as_float(vr[4 * c + 2]), __uint_as_float(vr[4 * c + 3]));
-        }
+      for (int c = 0; c < 4; ++c) {
+        *blk_chunk(dk_blk, row, 4 * wg + c) =
+            make_float4(__uint_as_float(kr[4 * c]) * p.scale, __uint_as_float(kr[4 * c + 1]) * p.scale,
+                        __uint_as_float(kr[4 * c + 2]) * p.scale, __uint_as_float(kr[4 * c + 3]) * p.scale);
+        *blk_chunk(dv_blk, row, 4 * wg + c) = make_float4(__uint_as_float(vr[4 * c]), __uint_as_float(vr[4 * c + 1]),
+                                                          __uint_as_float(vr[4 * c + 2]), __uint_as_float(vr[4 * c + 3]));
       }
     }
+    row_sync<kKvRowThreads>();
+    const int tile_rows = N - kt * kRows < kRows ? N - kt * kRows : kRows;
+    const int64_t off = (int64_t(bh) * N + kt * kRows) * D64;
+    if (ok && a.grad_k != nullptr) blk_copy_out(dk_blk, a.grad_k + off, tile_rows, tid, kKvRowThreads);
+    if (ok && a.grad_v != nullptr) blk_copy_out(dv_blk, a.grad_v + off, tile_rows, tid, kKvRowThreads);
   }
 
   tc_fence_before();
