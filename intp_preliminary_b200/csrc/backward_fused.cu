@@ -452,9 +452,19 @@ sla_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           // each cell of this warpgroup's array has one writer (this thread): a plain
           // read-add-write (measured faster than red.shared.add.f32 here)
           if (slotted) {
+            // in pairs: both cells are read before either is written (half the
+            // dependent read-add-write chain); a pair on one slot adds both values
+            // through the first element (the second stores the cell unchanged first)
+            const uint32_t ns = static_cast<uint32_t>(a.n_slots);
 #pragma unroll
-            for (int e2 = 0; e2 < 8; ++e2)
-              if (sl[e2] < static_cast<uint32_t>(a.n_slots)) drow[sl[e2] * kRows] += g[e2];
+            for (int e2 = 0; e2 < 8; e2 += 2) {
+              const uint32_t s0 = sl[e2], s1 = sl[e2 + 1];
+              const bool r0 = s0 < ns, r1 = s1 < ns, same = s0 == s1;
+              const float v0 = r0 ? drow[s0 * kRows] : 0.f;
+              const float v1 = r1 ? drow[s1 * kRows] : 0.f;
+              if (r1) drow[s1 * kRows] = v1 + (same ? 0.f : g[e2 + 1]);
+              if (r0) drow[s0 * kRows] = v0 + g[e2] + (same ? g[e2 + 1] : 0.f);
+            }
           }
         } else {
 #pragma unroll
