@@ -115,8 +115,9 @@ INTP_API intp_status svit_embed_post(const svit_embed_args* args, void* stream);
  * h's 12 poses consecutive).  args: directions == 6, look_poses == 12,
  * bases % 24 == 0, look_heads % 12 == 0, values == NULL, x and look_pose set;
  * resp and slot_fields are not used.  features % 8 == 0 (a ragged last
- * 64-wide K slab reads zeros).  `status`: the device int32 of the bounded
- * waits (as in sla_forward_args.status).                                     */
+ * 64-wide K slab reads zeros).  x, look_pose, pos_embed, cls and output_bias
+ * are 16-byte aligned (INTP_ERR_LAYOUT otherwise).  `status`: the device
+ * int32 of the bounded waits (as in sla_forward_args.status).                */
 INTP_API intp_status svit_tokenizer_gemm(const svit_embed_args* args, const void* patches, int64_t patches_stride,
                                          int32_t features, const void* weight, int32_t* status, void* stream);
 
