@@ -35,7 +35,7 @@ binning (it is defined by the benchmark description), so the fixture pins the
 reference's attention math on those inputs and the product's table builder is
 checked against the oracle separately.
 
-Run: python tests/golden/make_golden.py [--reference PATH] [--only dense_look_grid]
+Run: python tests/golden/make_golden.py --reference PATH [--only dense_look_grid]
 """
 
 from __future__ import annotations
