@@ -147,6 +147,39 @@ def test_tokenizer_gemm_matches_float64_and_unfused(model, cuda_device, batch):
     torch.testing.assert_close(pose, look_old.pose, atol=1e-2, rtol=0)
 
 
+@pytest.mark.parametrize("features", [200, 1680])
+def test_tokenizer_gemm_other_shapes(cuda_device, features):
+    """Shapes other than the model's: 48 bases (two tokenizer tiles), 12 Look
+    heads (one Look tile), 50 patches per image, 3 images = 150 rows (one
+    partial 256-row tile whose second half is short), random operands; the
+    float64 computation on the same bf16 values is the reference."""
+    gen = torch.Generator().manual_seed(31)
+    batch, n, bases, heads = 3, 50, 48, 12
+    dim = 2 * bases
+    patches = (torch.randn(batch * n, features, generator=gen) / 4).to(torch.bfloat16)
+    weight = (torch.randn(6 * bases + 12 * heads, features, generator=gen) / 4).to(torch.bfloat16)
+    p = dict(token_null=torch.randn(bases, generator=gen), direction_coef=torch.randn(6, 2, generator=gen),
+             output_bias=torch.randn(dim, generator=gen), cls=torch.randn(dim, generator=gen),
+             pos_embed=torch.randn(n + 1, dim, generator=gen), look_null=torch.randn(heads, generator=gen))
+    dev = {k: v.to(cuda_device) for k, v in p.items()}
+    x = torch.full((batch, n + 1, dim), float("nan"), device=cuda_device)
+    pose = torch.full((batch, n, heads, 12), float("nan"), device=cuda_device)
+    ops.tokenizer_gemm(patches.to(cuda_device), weight.to(cuda_device), batch=batch, patches_per_image=n,
+                       bases=bases, directions=6, look_heads=heads, look_poses=12, x=x, look_pose=pose, **dev)
+    resp = patches.double() @ weight.double().T
+    tok = resp[:, :6 * bases].reshape(batch, n, bases, 6)
+    tnull = p["token_null"].double()[None, None, :, None].expand(batch, n, bases, 1)
+    w = torch.cat((tok, tnull), -1).softmax(-1)[..., :-1]
+    tokens = torch.einsum("bnpd,dc->bnpc", w, p["direction_coef"].double()).reshape(batch, n, dim)
+    ref_x = torch.cat((p["cls"].double().expand(batch, 1, -1), tokens + p["output_bias"].double()), dim=1)
+    ref_x = ref_x + p["pos_embed"].double()
+    look = resp[:, 6 * bases:].reshape(batch, n, heads, 12)
+    lnull = p["look_null"].double()[None, None, :, None].expand(batch, n, heads, 1)
+    ref_pose = torch.cat((look, lnull), -1).softmax(-1)[..., :-1]
+    assert (x.cpu().double() - ref_x).abs().max().item() <= 1e-4
+    assert (pose.cpu().double() - ref_pose).abs().max().item() <= 1e-5
+
+
 def test_tokenizer_gemm_rejects_what_it_cannot_take(model, cuda_device):
     n = model.num_patches
     patches = torch.zeros(2 * n, 1680, dtype=torch.bfloat16, device=cuda_device)
