@@ -329,3 +329,50 @@ def test_tensor_core_backward_declines_other_inputs(cuda_device):
     assert grads[0].dtype == torch.float32
     with pytest.raises(ValueError):
         look_attention_backward(*dev[:3], out, lse, go, dev[3], slots, scale=0.125, kernel="tcgen05")
+
+
+@pytest.mark.parametrize("seq", [130, 300])
+def test_tensor_core_backward_without_look_bias(cuda_device, seq):
+    """The tensor-core backward's no-bias form (SLA_BIAS_NONE through the C ABI:
+    plain softmax attention, keys past the sequence masked) against float64
+    autograd; the forward's LSE comes from the same C call with the same
+    arguments.  Ragged query / key tiles at both lengths."""
+    import ctypes
+
+    from intp_preliminary_b200 import _lib
+    from intp_preliminary_b200.look_attention import _forward_args, _stride4
+
+    gen = torch.Generator().manual_seed(seq)
+    b, h = 2, 3
+    q, k, v = ((torch.randn(b, h, seq, 64, generator=gen) / 8).to(torch.bfloat16) for _ in range(3))
+    grad_out = torch.randn(b, h, seq, 64, generator=gen).to(torch.bfloat16)
+    slots = LookSlots(np.full((seq - 1, seq - 1), hexgrid.SLOT_NONE, dtype=np.uint8), 1)
+    pose = torch.zeros(b, seq - 1, h, 1)
+    dq_, dk_, dv_, go, pz = (t.to(cuda_device) for t in (q, k, v, grad_out, pose))
+    out = torch.empty_like(dq_)
+    lse = torch.empty(b, h, seq, device=cuda_device)
+    args, keep = _forward_args(dq_, dk_, dv_, pz, slots, 0.125, None, out, lse, "tcgen05")
+    args.bias_mode = _lib.SLA_BIAS_NONE
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    _lib.check(lib.sla_forward(ctypes.byref(args), stream), "forward")
+    f32 = dict(dtype=torch.float32, device=cuda_device)
+    grads = [torch.empty(b, h, seq, 64, **f32) for _ in range(3)]
+    delta = torch.empty(b, h, seq, **f32)
+    bwd = _lib.SlaBackwardArgs()
+    bwd.fwd = args
+    bwd.grad_out, bwd.grad_out_stride = go.data_ptr(), _stride4(go)
+    bwd.grad_q, bwd.grad_k, bwd.grad_v = (g.data_ptr() for g in grads)
+    bwd.grad_pose = bwd.grad_fields = bwd.grad_dense = None
+    bwd.delta = delta.data_ptr()
+    bwd.slots_packed_t = slots.device_packed_t(cuda_device).data_ptr()
+    _lib.check(lib.sla_backward(ctypes.byref(bwd), stream), "backward")
+    check_device_status(cuda_device)
+    del keep
+    leaves = [t.double().requires_grad_(True) for t in (q, k, v)]
+    ref = torch.softmax(leaves[0] @ leaves[1].transpose(-1, -2) * 0.125, dim=-1) @ leaves[2]
+    ref.backward(grad_out.double())
+    assert (out.cpu().double() - ref.detach()).abs().max().item() <= 2e-2 * ref.abs().max().item()
+    for got, leaf in zip(grads, leaves):
+        err = (got.cpu().double() - leaf.grad).abs().max().item()
+        assert err <= 2e-2 * max(leaf.grad.abs().max().item(), 1e-3), err
