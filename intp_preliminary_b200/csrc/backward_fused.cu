@@ -92,20 +92,6 @@ template <int RT>
 __device__ __forceinline__ void row_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(RT) : "memory");
 }
-// Row-thread barrier that also returns, to every row thread, whether any of them passed `v` true.
-template <int RT>
-__device__ __forceinline__ bool row_any(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "n"(RT)
-      : "memory");
-  return r != 0;
-}
 
 // A 128-row x 64-column fp32 gradient block staged in shared memory for the
 // epilogue: row r's 16-byte chunk c sits at chunk position c ^ (r & 15), so
